@@ -1,0 +1,422 @@
+#!/usr/bin/env python
+"""Benchmark of the B200 kernel backend (one JSON line on rank 0).
+
+Headline workload: C = A @ B, M = N = K = 4096, bf16 inputs ~ N(0,1)/sqrt(K),
+fp32 accumulation, bf16 output — the matmul configuration of the B200
+benchmark set, on the best configuration the search space offers for this
+backend (tcgen05, BLOCK_M 128, BLOCK_N 256, BLOCK_K 64, GROUP_M 8, 8 warps
+(persistent, warp-specialised), 4 stages).  One step = one matmul launch.
+Steps cycle over 4 independent input sets (4 x 96 MiB > 126 MB L2), so every
+launch streams its operands from HBM.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+N > 1 runs under torchrun, one process per GPU; every rank multiplies its
+own matrices (candidate evaluation shards with no exchange step), the
+timed region is bracketed by barriers + synchronize, and the max time over
+ranks is used.  ``value`` is whole-job TFLOP/s.  ``--impl reference`` times
+the reference's own CPU implementation of the path (its torch reference:
+fp32 matmul of the upcast operands) on the host cores, rank 0 only.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from datetime import timedelta
+
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+SHAPE = (4096, 4096, 4096)
+BEST = {"BLOCK_M": 128, "BLOCK_N": 256, "BLOCK_K": 64, "GROUP_M": 8, "num_warps": 8,
+        "num_stages": 4, "dtype": "bfloat16"}
+FLOPS = 2.0 * SHAPE[0] * SHAPE[1] * SHAPE[2]
+N_SETS = 4
+METRIC = "matmul_bf16_4096_tflops"
+# DRAM bytes (read + write) per launch of the headline kernel from one ncu
+# capture (profiles/matmul_tc_bf16_4096.md); None until captured.
+TRAFFIC_BYTES_PER_LAUNCH = None
+
+
+def parse_args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10000)
+    ap.add_argument("--warmup", type=int, default=50)
+    ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    ap.add_argument("--no-extras", action="store_true", help="skip per-task and search lines")
+    return ap.parse_args()
+
+
+# ------------------------------------------------------------ distributed
+def dist_init(n_gpus: int):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    elif torch.cuda.is_available():
+        torch.cuda.set_device(0)
+    return rank, world, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+
+
+def allreduce_max(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    import torch.distributed as dist
+
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def allreduce_sum(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    import torch.distributed as dist
+
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.SUM)
+    return float(t.item())
+
+
+# ----------------------------------------------------------------- clocks
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    REASONS = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+
+    def __init__(self, device: int) -> None:
+        self.proc = None
+        sel = []
+        try:
+            uuid = str(torch.cuda.get_device_properties(device).uuid)
+            sel = ["-i", uuid if uuid.startswith("GPU-") else f"GPU-{uuid}"]
+        except Exception:
+            pass
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", *sel, f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+
+    def stop(self) -> dict | None:
+        if self.proc is None:
+            return None
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=5)
+        except Exception:
+            self.proc.kill()
+            return None
+        sm, mx, reasons = [], 0.0, set()
+        for line in out.strip().splitlines():
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                s, m = float(f[1]), float(f[2])
+            except ValueError:
+                continue
+            mx = max(mx, m)
+            sm.append(s)
+            for name, val in zip(self.REASONS, f[5:9]):
+                if val.lower().startswith("active"):
+                    reasons.add(name)
+        if not sm:
+            return None
+        loaded = [s for s in sm if s > 0.5 * mx] or sm
+        return {"sm_mhz": statistics.median(loaded), "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ------------------------------------------------------------ our backend
+def run_ours(args, rank, world, local):
+    from gpu_optimizer_b200.harness import default_peaks
+    from gpu_optimizer_b200.runner import build_callable, check_device_status, warm_compile
+    from gpu_optimizer_b200.tasks import get_task
+
+    task = get_task("matmul", "b200")
+    sets = [task.make_inputs(SHAPE, "bfloat16", "cuda", seed=10 * i + rank)
+            for i in range(N_SETS)]
+    kcs = [build_callable("matmul", SHAPE, BEST, s) for s in sets]
+    for kc in kcs:
+        warm_compile(kc)
+    stream = torch.cuda.current_stream()
+    for i in range(args.warmup):
+        kcs[i % N_SETS].fn()
+    torch.cuda.synchronize()
+    check_device_status()
+
+    clocks = ClockSampler(local)
+    time.sleep(0.3)
+    barrier(world)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for i in range(args.steps):
+        kcs[i % N_SETS].fn()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    barrier(world)
+    ms = e0.elapsed_time(e1)
+    clk = clocks.stop()
+    check_device_status()
+    ms_max = allreduce_max(ms, world)
+    ms_per_step = ms_max / args.steps
+    value = world * args.steps * FLOPS / (ms_max * 1e-3) / 1e12
+    per_launch_ms = ms / args.steps
+    achieved = FLOPS / (per_launch_ms * 1e-3) / 1e12
+    peaks = default_peaks()
+    peak = peaks["bf16_tflops"]
+
+    # correctness of the measured kernel (last output vs the device reference)
+    from gpu_optimizer_b200.correctness import check_correctness
+
+    out = kcs[0].fn()
+    rep = check_correctness(out, task.reference(*sets[0]), *task.tolerance("bfloat16"))
+
+    e2e = measure_e2e(args, world, task)
+
+    line = {
+        "metric": METRIC, "value": round(value, 2), "unit": "TFLOP/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 5),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic: seeded N(0,1)/sqrt(K) bf16 operands, 4 rotating input sets",
+        "config": {"workload": "matmul bf16 M=N=K=4096, fp32 accumulate, bf16 out",
+                   "candidate": BEST, "kernel": kcs[0].launch["kernel"],
+                   "l2": "4 rotating input sets of 96 MiB (384 MiB > 126 MB L2)",
+                   "parallelism": f"independent per-GPU problems x{world} (no collective)"},
+        "roofline": {"bound": "tensor", "achieved": round(achieved, 2), "peak": peak,
+                     "unit": "TFLOP/s", "frac": round(achieved / peak, 4),
+                     "peak_source": f"{peaks['source']} (MEASURED_PEAKS.json bf16_tflops burst)"
+                     if peaks["source"] == "measured" else "fallback 1590 TFLOP/s",
+                     "traffic": TRAFFIC_BYTES_PER_LAUNCH,
+                     "algorithmic_flops_per_launch": FLOPS},
+        "e2e": e2e,
+        "gpu_launches": args.steps,
+        "clocks": clk,
+        "correctness": {"passed": rep.passed, "max_abs_err": rep.max_abs_err,
+                        "rel_err_floored": rep.rel_err_floored},
+    }
+    return line
+
+
+def measure_e2e(args, world, task):
+    """Same metric through build_callable/fn with pinned host operands:
+    every step copies A and B host->device, runs, and reads C back."""
+    from gpu_optimizer_b200.runner import build_callable
+
+    a_h, b_h = (t.cpu().pin_memory() for t in task.make_inputs(SHAPE, "bfloat16", "cpu", 99))
+    a_d, b_d = torch.empty_like(a_h, device="cuda"), torch.empty_like(b_h, device="cuda")
+    kc = build_callable("matmul", SHAPE, BEST, (a_d, b_d))
+    c_h = torch.empty(SHAPE[0], SHAPE[1], dtype=torch.bfloat16).pin_memory()
+    steps = max(10, min(args.steps, 200))
+
+    def step():
+        a_d.copy_(a_h, non_blocking=True)
+        b_d.copy_(b_h, non_blocking=True)
+        c = kc.fn()
+        c_h.copy_(c, non_blocking=True)
+
+    for _ in range(3):
+        step()
+    torch.cuda.synchronize()
+    barrier(world)
+    s = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(s)
+    for _ in range(steps):
+        step()
+    e1.record(s)
+    torch.cuda.synchronize()
+    ms = allreduce_max(e0.elapsed_time(e1), world)
+    return {"value": round(world * steps * FLOPS / (ms * 1e-3) / 1e12, 2), "unit": "TFLOP/s",
+            "h2d_bytes_per_step": a_h.numel() * 2 + b_h.numel() * 2,
+            "d2h_bytes_per_step": c_h.numel() * 2, "steps": steps}
+
+
+# ------------------------------------------------------------ CPU legs
+def cpu_matmul_sample(rows: int, seconds: float):
+    """The reference's CPU path (fp32 matmul of upcast bf16 operands,
+    benchmarks/matmul/task.py:32-34) on a row slice of the workload."""
+    from oracle import reference as O
+
+    a, b = O.make_inputs("matmul", SHAPE, "bfloat16", 0, profile="b200")
+    a = a[:rows].contiguous()
+    torch.set_num_threads(os.cpu_count() or 1)
+    O.reference("matmul", (a, b))  # warm-up
+    n, t0 = 0, time.perf_counter()
+    while True:
+        O.reference("matmul", (a, b))
+        n += 1
+        el = time.perf_counter() - t0
+        if el >= seconds:
+            break
+    flops = 2.0 * rows * SHAPE[1] * SHAPE[2] * n
+    return flops / el / 1e12, n, el
+
+
+def cpu_baseline():
+    rows = 256
+    v, n, el = cpu_matmul_sample(rows, 10.0)
+    return {"value": round(v, 4), "unit": "TFLOP/s", "cores": os.cpu_count(), "kind": "port",
+            "sample": f"{n} x ({rows}x4096 rows of A) @ B(4096x4096), fp32 upcast, "
+                      f"{el:.1f} s, torch CPU with {os.cpu_count()} threads"}
+
+
+def run_reference(args, rank, world):
+    if rank != 0:
+        return None
+    # size each step so the whole run stays within about a minute
+    v1, _, el1 = cpu_matmul_sample(16, 0.5)
+    per_row = 2.0 * SHAPE[1] * SHAPE[2] / (v1 * 1e12)
+    budget = 60.0 / max(1, args.steps + args.warmup)
+    rows = int(max(1, min(SHAPE[0], budget / per_row)))
+    from oracle import reference as O
+
+    a, b = O.make_inputs("matmul", SHAPE, "bfloat16", 0, profile="b200")
+    a = a[:rows].contiguous()
+    torch.set_num_threads(os.cpu_count() or 1)
+    for _ in range(args.warmup):
+        O.reference("matmul", (a, b))
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        O.reference("matmul", (a, b))
+    el = time.perf_counter() - t0
+    value = args.steps * 2.0 * rows * SHAPE[1] * SHAPE[2] / el / 1e12
+    sample = (f"each step: {rows} rows of A (4096x4096 bf16 upcast to fp32) @ B, "
+              f"torch CPU fp32 matmul, {os.cpu_count()} threads")
+    return {
+        "metric": METRIC, "value": round(value, 4), "unit": "TFLOP/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(el * 1e3 / args.steps, 4), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": "matmul bf16 M=N=K=4096 (row sample per step)"},
+        "impl": "reference",
+        "cpu_baseline": {"value": round(value, 4), "unit": "TFLOP/s", "cores": os.cpu_count(),
+                         "kind": "port", "sample": sample},
+        "e2e": {"value": round(value, 4), "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+
+
+# ------------------------------------------------------------ extras
+EXTRA_TASKS = [
+    ("vecadd", (1 << 24,), {"BLOCK_SIZE": 4096, "num_warps": 8, "dtype": "float32"}),
+    ("softmax", (16384, 8192), {"BLOCK_N": 8192, "num_warps": 8, "num_stages": 1,
+                                "dtype": "bfloat16"}),
+    ("layernorm", (16384, 8192), {"BLOCK_N": 8192, "num_warps": 8, "num_stages": 1,
+                                  "dtype": "bfloat16"}),
+    ("reduction", (1 << 28,), {"BLOCK_SIZE": 8192, "num_warps": 16, "strategy": "atomic",
+                               "dtype": "float32"}),
+    ("fused_gelu", (1 << 26,), {"BLOCK_SIZE": 4096, "num_warps": 8, "strategy": "fused",
+                                "dtype": "bfloat16"}),
+    ("attention_causal", (128, 4096, 128), {"BLOCK_M": 128, "BLOCK_N": 128, "num_warps": 4,
+                                            "num_stages": 2, "dtype": "bfloat16"}),
+    ("matmul", (8192, 8192, 8192), BEST),
+]
+
+
+def run_extras(world):
+    from gpu_optimizer_b200.harness import BenchmarkSettings, CudaBenchmarkEngine
+    from gpu_optimizer_b200.tasks import get_task
+
+    eng = CudaBenchmarkEngine(settings=BenchmarkSettings(warmup=5, iterations=20, flush_l2=True,
+                                                         cache_inputs=1))
+    out = {}
+    for name, shape, cfg in EXTRA_TASKS:
+        task = get_task(name, "b200")
+        try:
+            r = eng.benchmark_candidate(task, task.make_candidate(shape, cfg))
+            out[f"{name}{list(shape)}"] = {
+                "status": r.status, "kernel": r.kernel, "config": cfg,
+                "median_ms": round(r.latency.median_ms, 4) if r.ok else None,
+                "achieved": round(r.achieved, 1), "unit": r.achieved_unit,
+                "frac_of_measured_peak": round(r.roofline_fraction, 4),
+                "rel_err_floored": r.correctness.rel_err_floored if r.correctness else None,
+                "error": r.error[:200]}
+        except Exception as e:  # keep the headline line alive
+            out[f"{name}{list(shape)}"] = {"status": "error", "error": str(e)[:200]}
+        torch.cuda.empty_cache()
+    return out
+
+
+def run_search(world, rank):
+    """Candidates evaluated per second over a fixed per-GPU batch of the B200
+    matmul space (weak scaling: each rank evaluates its own 12 candidates)."""
+    import random
+
+    from gpu_optimizer_b200.harness import BenchmarkSettings, CudaBenchmarkEngine
+    from gpu_optimizer_b200.tasks import get_task
+
+    task = get_task("matmul", "b200")
+    shape = (2048, 2048, 2048)
+    eng = CudaBenchmarkEngine(settings=BenchmarkSettings(warmup=5, iterations=20))
+    space = task.param_space(shape)
+    rng = random.Random(1000 + rank)
+    cands = [task.make_candidate(shape, space.sample(rng), "random") for _ in range(12)]
+    eng.benchmark_candidate(task, cands[0])  # inputs + reference cached
+    barrier(world)
+    t0 = time.perf_counter()
+    st = [eng.benchmark_candidate(task, c).status for c in cands]
+    el = allreduce_max(time.perf_counter() - t0, world)
+    n = allreduce_sum(len(cands), world)
+    return {"candidates_per_s": round(n / el, 2), "candidates": int(n), "seconds": round(el, 2),
+            "shape": list(shape), "statuses": {s: st.count(s) for s in set(st)}}
+
+
+def main():
+    args = parse_args()
+    rank, world, local = dist_init(args.gpus)
+    if args.impl == "reference":
+        line = run_reference(args, rank, world)
+        if rank == 0 and line is not None:
+            print(json.dumps(line), flush=True)
+        return
+    line = run_ours(args, rank, world, local)
+    if not args.no_extras:
+        try:
+            line["search"] = run_search(world, rank)
+        except Exception as e:
+            line["search"] = {"error": str(e)[:200]}
+        if world == 1:
+            line["tasks"] = run_extras(world)
+    if rank == 0 and world == 1:
+        line["cpu_baseline"] = cpu_baseline()
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,502 @@
+// Flash-attention forward on tcgen05 tensor cores (sm_100a), non-causal and
+// causal.
+//
+// Replaces attention_kernel (compiler/triton/kernels.py:212-270) for 16-bit
+// inputs with BLOCK_M = 128.  One CTA per (128-row query tile, batch*head);
+// causal grids visit the longest query tiles first.
+//
+// Warp roles (8 warps):
+//   warp 0  TMA producer: Q once, then K_j and V_j into a num_stages ring.
+//   warp 1  MMA issuer:   S_j = Q K_j^T into TMEM buffer j%2, then
+//                         O += P_{j-1} V_{j-1} (one block behind, so the
+//                         softmax of block j overlaps S_{j+1} and PV_{j-1}).
+//   warp 2  TMEM owner.
+//   warps 4-7 softmax / correction / epilogue: thread r owns query row r
+//           (TMEM lane r).  It reads S_j from TMEM, applies scale, padding
+//           and causal masks, keeps the running max in the log2 domain,
+//           writes P_j = exp2(s - m) as 16-bit values into a swizzled shared
+//           buffer (the A operand of the PV MMA) and accumulates the fp32
+//           row sum.  The running max used for P is only moved (and O in
+//           TMEM rescaled) when a block's max exceeds it by more than 8
+//           (a factor of 256); until then P <= 256, which 16-bit P and the
+//           fp32 accumulator represent exactly as well as P <= 1.
+// TMEM columns: O [0, D), S buffers [D, D+BN) and [D+BN, D+2BN).
+#include <algorithm>
+
+#include "gpo_common.cuh"
+#include "gpo_internal.h"
+
+namespace gpo {
+
+constexpr int kAttnMaxStages = 4;
+constexpr float kRescaleThreshold = 8.0f;
+
+struct AttnShared {
+  uint64_t q_full;
+  uint64_t k_full[kAttnMaxStages];
+  uint64_t v_full[kAttnMaxStages];
+  uint64_t kv_empty[kAttnMaxStages];
+  uint64_t s_full[2];
+  uint64_t s_free[2];
+  uint64_t p_full[2];
+  uint64_t pv_done[2];
+  uint64_t drain;
+  uint32_t tmem_base;
+  int abort;
+};
+
+__host__ __device__ constexpr int attn_tmem_alloc(int cols) {
+  return cols <= 32 ? 32 : cols <= 64 ? 64 : cols <= 128 ? 128 : cols <= 256 ? 256 : 512;
+}
+
+// Byte offset of 16-byte chunk `chunk` of row `row` inside a K-major
+// swizzled tile of 128 rows whose rows are split into atoms of `sw` bytes.
+__device__ __forceinline__ uint32_t kmajor_swizzled(int row, int byte_in_row, int sw) {
+  const uint32_t atom = static_cast<uint32_t>(byte_in_row / sw);
+  const uint32_t off = atom * (128u * sw) + static_cast<uint32_t>(row) * sw +
+                       static_cast<uint32_t>(byte_in_row % sw);
+  return off ^ (((off >> 7) & static_cast<uint32_t>(sw / 16 - 1)) << 4);
+}
+
+template <typename T, int FMT, int BN, int D, bool CAUSAL>
+__global__ void __launch_bounds__(256, 1)
+    attn_tc_kernel(const __grid_constant__ CUtensorMap tma_q,
+                   const __grid_constant__ CUtensorMap tma_k,
+                   const __grid_constant__ CUtensorMap tma_v, T* __restrict__ O, int S,
+                   int stages, float scale_log2, unsigned int* err) {
+  constexpr int ES = 2;
+  constexpr int SWQ = (D * ES) < 128 ? (D * ES) : 128;  // swizzle of Q/K/V rows
+  constexpr int SWP = (BN * ES) < 128 ? (BN * ES) : 128;  // swizzle of P rows
+  constexpr uint32_t Q_BYTES = 128u * D * ES;
+  constexpr uint32_t KV_BYTES = static_cast<uint32_t>(BN) * D * ES;
+  constexpr uint32_t P_BYTES = 128u * BN * ES;
+  constexpr int COLS = D + 2 * BN;
+  constexpr int ALLOC = attn_tmem_alloc(COLS);
+  constexpr uint32_t IDESC_S = make_idesc(FMT, 128, BN, false, false);
+  constexpr uint32_t IDESC_O = make_idesc(FMT, 128, D, false, true);
+
+  __shared__ AttnShared sh;
+  extern __shared__ uint8_t dyn_smem[];
+  const uint32_t base = (smem_u32(dyn_smem) + 1023u) & ~1023u;
+  const uint32_t q_smem = base;
+  const uint32_t p_smem = q_smem + Q_BYTES;                 // 2 buffers
+  const uint32_t kv_smem = p_smem + 2 * ((P_BYTES + 1023u) & ~1023u);
+  const uint32_t kv_stage = 2 * ((KV_BYTES + 1023u) & ~1023u);
+  const uint32_t p_stride = (P_BYTES + 1023u) & ~1023u;
+  const uint32_t v_off = (KV_BYTES + 1023u) & ~1023u;
+  uint8_t* p_generic = dyn_smem + (p_smem - smem_u32(dyn_smem));
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int num_q_tiles = (S + 127) / 128;
+  // longest causal rows first; identity order for the non-causal task
+  const int qt = CAUSAL ? (num_q_tiles - 1 - static_cast<int>(blockIdx.x))
+                        : static_cast<int>(blockIdx.x);
+  const int q0 = qt * 128;
+  const int bh = blockIdx.y;
+  const int kv_len = CAUSAL ? min(S, q0 + 128) : S;
+  const int nblk = (kv_len + BN - 1) / BN;
+
+  if (threadIdx.x == 0) {
+    mbar_init(smem_u32(&sh.q_full), 1);
+    for (int s = 0; s < stages; ++s) {
+      mbar_init(smem_u32(&sh.k_full[s]), 1);
+      mbar_init(smem_u32(&sh.v_full[s]), 1);
+      mbar_init(smem_u32(&sh.kv_empty[s]), 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(smem_u32(&sh.s_full[b]), 1);
+      mbar_init(smem_u32(&sh.s_free[b]), 4);
+      mbar_init(smem_u32(&sh.p_full[b]), 4);
+      mbar_init(smem_u32(&sh.pv_done[b]), 1);
+    }
+    mbar_init(smem_u32(&sh.drain), 1);
+    sh.abort = 0;
+    fence_barrier_init();
+    tma_prefetch_desc(&tma_q);
+    tma_prefetch_desc(&tma_k);
+    tma_prefetch_desc(&tma_v);
+  }
+  if (warp == 2) {
+    tmem_alloc(smem_u32(&sh.tmem_base), ALLOC);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = sh.tmem_base;
+  const uint32_t o_tmem = tmem;
+  volatile int* abort_flag = &sh.abort;
+
+  if (warp == 0 && lane == 0) {
+    // ------------------------------------------------------------ producer
+    bool ok = true;
+    int issued = 0;
+    mbar_arrive_expect_tx(smem_u32(&sh.q_full), Q_BYTES);
+#pragma unroll
+    for (int a = 0; a < (D * ES) / SWQ; ++a)
+      tma_load_3d(q_smem + a * 128 * SWQ, &tma_q, smem_u32(&sh.q_full), a * (SWQ / ES), q0, bh);
+    for (int j = 0; j < nblk; ++j) {
+      const int s = j % stages;
+      const uint32_t r = static_cast<uint32_t>(j / stages);
+      if (!mbar_wait(smem_u32(&sh.kv_empty[s]), (r & 1u) ^ 1u, abort_flag, err,
+                     kErrWaitProducer)) {
+        ok = false;
+        break;
+      }
+      const uint32_t ks = kv_smem + s * kv_stage;
+      const uint32_t kf = smem_u32(&sh.k_full[s]), vf = smem_u32(&sh.v_full[s]);
+      mbar_arrive_expect_tx(kf, KV_BYTES);
+#pragma unroll
+      for (int a = 0; a < (D * ES) / SWQ; ++a)
+        tma_load_3d(ks + a * BN * SWQ, &tma_k, kf, a * (SWQ / ES), j * BN, bh);
+      mbar_arrive_expect_tx(vf, KV_BYTES);
+#pragma unroll
+      for (int a = 0; a < (D * ES) / SWQ; ++a)
+        tma_load_3d(ks + v_off + a * BN * SWQ, &tma_v, vf, a * (SWQ / ES), j * BN, bh);
+      issued = j + 1;
+    }
+    if (!ok) {
+      mbar_wait_drain(smem_u32(&sh.q_full), 0, err);
+      for (int j = max(0, issued - stages); j < issued; ++j) {
+        mbar_wait_drain(smem_u32(&sh.k_full[j % stages]), static_cast<uint32_t>(j / stages) & 1u,
+                        err);
+        mbar_wait_drain(smem_u32(&sh.v_full[j % stages]), static_cast<uint32_t>(j / stages) & 1u,
+                        err);
+      }
+    }
+  } else if (warp == 1 && lane == 0) {
+    // ---------------------------------------------------------- MMA issuer
+    bool ok = mbar_wait(smem_u32(&sh.q_full), 0, abort_flag, err, kErrWaitMma);
+    auto issue_pv = [&](int i) -> bool {
+      const int s = i % stages;
+      const uint32_t r = static_cast<uint32_t>(i / stages);
+      const int b = i & 1;
+      const uint32_t u = static_cast<uint32_t>(i >> 1);
+      if (!mbar_wait(smem_u32(&sh.p_full[b]), u & 1u, abort_flag, err, kErrWaitMma)) return false;
+      if (!mbar_wait(smem_u32(&sh.v_full[s]), r & 1u, abort_flag, err, kErrWaitMma)) return false;
+      tc_fence_after();
+      const uint32_t pb = p_smem + b * p_stride;
+      const uint32_t vs = kv_smem + s * kv_stage + v_off;
+#pragma unroll
+      for (int kk = 0; kk < BN / 16; ++kk) {
+        const uint32_t kbyte = static_cast<uint32_t>(kk) * 32u;
+        const uint64_t adesc =
+            make_smem_desc(pb + (kbyte / SWP) * (128 * SWP) + (kbyte % SWP), 16, 8 * SWP, SWP);
+        const uint64_t bdesc = make_smem_desc(vs + kk * 16 * SWQ, BN * SWQ, 8 * SWQ, SWQ);
+        mma_f16_ss(o_tmem, adesc, bdesc, IDESC_O, (i > 0 || kk > 0) ? 1u : 0u);
+      }
+      mma_commit(smem_u32(&sh.kv_empty[s]));
+      mma_commit(smem_u32(&sh.pv_done[b]));
+      return true;
+    };
+    // With a single K/V stage, K_j can only land after PV_{j-1} frees the
+    // stage, so PV_{j-1} is issued before S_j instead of after it.
+    const bool pv_first = stages == 1;
+    for (int j = 0; j < nblk && ok; ++j) {
+      const int s = j % stages;
+      const uint32_t r = static_cast<uint32_t>(j / stages);
+      const int b = j & 1;
+      const uint32_t u = static_cast<uint32_t>(j >> 1);
+      if (pv_first && j > 0 && !issue_pv(j - 1)) {
+        ok = false;
+        break;
+      }
+      if (!mbar_wait(smem_u32(&sh.k_full[s]), r & 1u, abort_flag, err, kErrWaitMma) ||
+          !mbar_wait(smem_u32(&sh.s_free[b]), (u & 1u) ^ 1u, abort_flag, err, kErrWaitMma)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const uint32_t ks = kv_smem + s * kv_stage;
+      const uint32_t s_tmem = tmem + static_cast<uint32_t>(D + b * BN);
+#pragma unroll
+      for (int kk = 0; kk < D / 16; ++kk) {
+        const uint32_t kbyte = static_cast<uint32_t>(kk) * 32u;
+        const uint32_t aoff = (kbyte / SWQ) * (128 * SWQ) + (kbyte % SWQ);
+        const uint32_t boff = (kbyte / SWQ) * (BN * SWQ) + (kbyte % SWQ);
+        const uint64_t adesc = make_smem_desc(q_smem + aoff, 16, 8 * SWQ, SWQ);
+        const uint64_t bdesc = make_smem_desc(ks + boff, 16, 8 * SWQ, SWQ);
+        mma_f16_ss(s_tmem, adesc, bdesc, IDESC_S, kk > 0 ? 1u : 0u);
+      }
+      mma_commit(smem_u32(&sh.s_full[b]));
+      if (!pv_first && j > 0 && !issue_pv(j - 1)) {
+        ok = false;
+        break;
+      }
+    }
+    if (ok && nblk > 0) ok = issue_pv(nblk - 1);
+    if (!ok) {
+      mma_commit(smem_u32(&sh.drain));
+      mbar_wait_drain(smem_u32(&sh.drain), 0, err);
+    }
+  } else if (warp >= 4) {
+    // ------------------------------------------- softmax / correction / epilogue
+    const int q = warp & 3;
+    const int row = q * 32 + lane;  // query row within the tile == TMEM lane
+    const int qrow = q0 + row;
+    const uint32_t lane_addr = static_cast<uint32_t>(q * 32) << 16;
+    float m_used = -INFINITY;
+    float l = 0.f;
+    bool ok = true;
+    for (int j = 0; j < nblk; ++j) {
+      const int b = j & 1;
+      const uint32_t u = static_cast<uint32_t>(j >> 1);
+      if (!mbar_wait(smem_u32(&sh.s_full[b]), u & 1u, abort_flag, err, kErrWaitSoftmax)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      float sv[BN];
+#pragma unroll
+      for (int c = 0; c < BN / 32; ++c) {
+        uint32_t r[32];
+        tmem_ld32(tmem + lane_addr + static_cast<uint32_t>(D + b * BN + c * 32), r);
+        tmem_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 32; ++i) sv[c * 32 + i] = __uint_as_float(r[i]);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_u32(&sh.s_free[b]));
+
+      // scale into the log2 domain and mask padding / future keys
+      const int key0 = j * BN;
+      float mb = -INFINITY;
+#pragma unroll
+      for (int i = 0; i < BN; ++i) {
+        const int key = key0 + i;
+        const bool masked = key >= S || (CAUSAL && key > qrow);
+        sv[i] = masked ? -INFINITY : sv[i] * scale_log2;
+        mb = fmaxf(mb, sv[i]);
+      }
+      if (j == 0) {
+        m_used = mb;
+      } else {
+        const bool need = mb > m_used + kRescaleThreshold;
+        if (__any_sync(0xffffffffu, need)) {
+          const float m_new = need ? mb : m_used;
+          const float alpha = ex2_approx(m_used - m_new);
+          // O holds PV_0..PV_{j-1}; wait for PV_{j-1} before rescaling it
+          const int pj = j - 1;
+          if (!mbar_wait(smem_u32(&sh.pv_done[pj & 1]), static_cast<uint32_t>(pj >> 1) & 1u,
+                         abort_flag, err, kErrWaitSoftmax)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+#pragma unroll 1
+          for (int c = 0; c < D / 32; ++c) {
+            uint32_t r[32];
+            const uint32_t addr = o_tmem + lane_addr + static_cast<uint32_t>(c * 32);
+            tmem_ld32(addr, r);
+            tmem_wait_ld();
+#pragma unroll
+            for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha);
+            tmem_st32(addr, r);
+          }
+          tmem_wait_st();
+          l *= alpha;
+          m_used = m_new;
+        }
+      }
+      // P_j = exp2(s - m_used); the P buffer b is free once PV_{j-2} is done
+      float rs = 0.f;
+#pragma unroll
+      for (int i = 0; i < BN; ++i) {
+        sv[i] = (m_used == -INFINITY) ? 0.f : ex2_approx(sv[i] - m_used);
+        rs += sv[i];
+      }
+      l += rs;
+      if (j >= 2) {
+        const int pj = j - 2;
+        if (!mbar_wait(smem_u32(&sh.pv_done[pj & 1]), static_cast<uint32_t>(pj >> 1) & 1u,
+                       abort_flag, err, kErrWaitSoftmax)) {
+          ok = false;
+          break;
+        }
+      }
+      uint8_t* pbuf = p_generic + b * p_stride;
+#pragma unroll
+      for (int g = 0; g < BN / 8; ++g) {
+        uint4 v4;
+        if constexpr (FMT == 1) {
+          v4 = make_uint4(pack_bf16(sv[8 * g], sv[8 * g + 1]), pack_bf16(sv[8 * g + 2], sv[8 * g + 3]),
+                          pack_bf16(sv[8 * g + 4], sv[8 * g + 5]),
+                          pack_bf16(sv[8 * g + 6], sv[8 * g + 7]));
+        } else {
+          v4 = make_uint4(pack_f16(sv[8 * g], sv[8 * g + 1]), pack_f16(sv[8 * g + 2], sv[8 * g + 3]),
+                          pack_f16(sv[8 * g + 4], sv[8 * g + 5]),
+                          pack_f16(sv[8 * g + 6], sv[8 * g + 7]));
+        }
+        *reinterpret_cast<uint4*>(pbuf + kmajor_swizzled(row, g * 16, SWP)) = v4;
+      }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_u32(&sh.p_full[b]));
+    }
+    // ------------------------------------------------------------ epilogue
+    if (ok && nblk > 0) {
+      const int pj = nblk - 1;
+      ok = mbar_wait(smem_u32(&sh.pv_done[pj & 1]), static_cast<uint32_t>(pj >> 1) & 1u,
+                     abort_flag, err, kErrWaitSoftmax);
+    }
+    if (ok) {
+      tc_fence_after();
+      const float inv_l = l > 0.f ? 1.0f / l : 0.f;
+      T* orow = O + (static_cast<int64_t>(bh) * S + qrow) * D;
+#pragma unroll 1
+      for (int c = 0; c < D / 32; ++c) {
+        uint32_t r[32];
+        tmem_ld32(o_tmem + lane_addr + static_cast<uint32_t>(c * 32), r);
+        tmem_wait_ld();
+        if (qrow < S) {
+          uint32_t pk[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const float lo = __uint_as_float(r[2 * i]) * inv_l;
+            const float hi = __uint_as_float(r[2 * i + 1]) * inv_l;
+            pk[i] = FMT == 1 ? pack_bf16(lo, hi) : pack_f16(lo, hi);
+          }
+          uint4* d4 = reinterpret_cast<uint4*>(orow + c * 32);
+#pragma unroll
+          for (int i = 0; i < 4; ++i)
+            d4[i] = make_uint4(pk[4 * i], pk[4 * i + 1], pk[4 * i + 2], pk[4 * i + 3]);
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 2) tmem_dealloc(tmem, ALLOC);
+}
+
+// ------------------------------------------------------------------- host
+typedef CUresult (*EncodeTiledFn3)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+// (BH, S, D) tensor as a 3-D map {D, S, BH} with box {sw/es, rows, 1}.
+static bool encode_bsd(CUtensorMap* map, CUtensorMapDataType dt, const void* ptr, uint64_t BH,
+                       uint64_t S, uint64_t D, uint32_t rows, int sw) {
+  EncodeTiledFn3 fn = reinterpret_cast<EncodeTiledFn3>(tensor_map_encoder());
+  if (!fn) return false;
+  const cuuint64_t dims[3] = {D, S, BH};
+  const cuuint64_t strides[2] = {D * 2, S * D * 2};
+  const cuuint32_t box[3] = {static_cast<cuuint32_t>(sw / 2), rows, 1};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  const CUtensorMapSwizzle swz = sw == 128  ? CU_TENSOR_MAP_SWIZZLE_128B
+                                 : sw == 64 ? CU_TENSOR_MAP_SWIZZLE_64B
+                                            : CU_TENSOR_MAP_SWIZZLE_32B;
+  return fn(map, dt, 3, const_cast<void*>(ptr), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+static uint32_t attn_tc_smem(int BN, int D, int stages) {
+  auto al = [](uint32_t x) { return (x + 1023u) & ~1023u; };
+  const uint32_t q = 128u * D * 2, p = 128u * BN * 2, kv = static_cast<uint32_t>(BN) * D * 2;
+  return al(q) + 2 * al(p) + static_cast<uint32_t>(stages) * 2 * al(kv) + 1024u;
+}
+
+// Plan: aux[0] = dynamic smem bytes.
+gpo_status plan_attention_tc(const gpo_key& k, Plan& p, std::string& log) {
+  const int D = static_cast<int>(k.shape[2]);
+  const int BN = k.block_n;
+  if (k.num_stages < 1 || k.num_stages > kAttnMaxStages) {
+    log = "num_stages must be in [1, 4]";
+    return GPO_BAD_CONFIG;
+  }
+  const uint32_t dyn = attn_tc_smem(BN, D, k.num_stages);
+  const uint32_t smem = dyn + static_cast<uint32_t>(sizeof(AttnShared));
+  if (smem > kMaxSmemPerCta) {
+    log = "shared memory " + std::to_string(smem) + " B (Q, 2 P buffers, " +
+          std::to_string(k.num_stages) + " K/V stages) exceeds the 232448 B per-CTA limit";
+    return GPO_COMPILE_ERROR;
+  }
+  const int cols = attn_tmem_alloc(D + 2 * BN);
+  if (D + 2 * BN > static_cast<int>(kTmemCols)) {
+    log = "TMEM needs " + std::to_string(D + 2 * BN) + " columns > 512";
+    return GPO_COMPILE_ERROR;
+  }
+  p.aux[0] = static_cast<int>(dyn);
+  p.family = "attn_tc";
+  p.res.smem_bytes = smem;
+  p.res.tmem_cols = static_cast<uint32_t>(cols);
+  p.res.threads_per_cta = 256;
+  p.res.grid_x = static_cast<uint32_t>(cdiv(k.shape[1], 128));
+  p.res.grid_y = static_cast<uint32_t>(k.shape[0]);
+  p.res.grid_z = 1;
+  p.res.launches_per_call = 1;
+  snprintf(p.res.kernel, sizeof(p.res.kernel), "attn_tc_kernel<%s,BN=%d,D=%d,%s>",
+           k.dtype == GPO_BFLOAT16 ? "bf16" : "f16", BN, D,
+           k.task == GPO_TASK_ATTENTION_CAUSAL ? "causal" : "full");
+  return GPO_OK;
+}
+
+template <typename T, int FMT, int BN, int D, bool CAUSAL>
+static gpo_status run_attn_tc(const gpo_key& k, const Plan& p, const gpo_args& a,
+                              const LaunchCtx& c, CUtensorMapDataType dt) {
+  const uint64_t BH = static_cast<uint64_t>(k.shape[0]), S = static_cast<uint64_t>(k.shape[1]);
+  constexpr int SW = (D * 2) < 128 ? (D * 2) : 128;
+  CUtensorMap mq, mk, mv;
+  if (!encode_bsd(&mq, dt, a.in[0], BH, S, D, 128, SW) ||
+      !encode_bsd(&mk, dt, a.in[1], BH, S, D, BN, SW) ||
+      !encode_bsd(&mv, dt, a.in[2], BH, S, D, BN, SW))
+    return GPO_LAUNCH_ERROR;
+  auto kern = attn_tc_kernel<T, FMT, BN, D, CAUSAL>;
+  const uint32_t dyn = static_cast<uint32_t>(p.aux[0]);
+  gpo_status s = ensure_smem_attr(reinterpret_cast<const void*>(kern), dyn);
+  if (s != GPO_OK) return s;
+  const dim3 grid(static_cast<unsigned>(cdiv(S, 128)), static_cast<unsigned>(BH));
+  const float scale_log2 = 1.4426950408889634f / sqrtf(static_cast<float>(D));
+  kern<<<grid, 256, dyn, c.stream>>>(mq, mk, mv, static_cast<T*>(a.out), static_cast<int>(S),
+                                     k.num_stages, scale_log2, c.err);
+  return launch_status();
+}
+
+template <typename T, int FMT, int BN, bool CAUSAL>
+static gpo_status run_attn_tc_d(const gpo_key& k, const Plan& p, const gpo_args& a,
+                                const LaunchCtx& c, CUtensorMapDataType dt) {
+  switch (k.shape[2]) {
+    case 32: return run_attn_tc<T, FMT, BN, 32, CAUSAL>(k, p, a, c, dt);
+    case 64: return run_attn_tc<T, FMT, BN, 64, CAUSAL>(k, p, a, c, dt);
+    case 128: return run_attn_tc<T, FMT, BN, 128, CAUSAL>(k, p, a, c, dt);
+    case 256: return run_attn_tc<T, FMT, BN, 256, CAUSAL>(k, p, a, c, dt);
+    default: return GPO_INTERNAL;
+  }
+}
+
+template <typename T, int FMT, bool CAUSAL>
+static gpo_status run_attn_tc_bn(const gpo_key& k, const Plan& p, const gpo_args& a,
+                                 const LaunchCtx& c, CUtensorMapDataType dt) {
+  switch (k.block_n) {
+    case 32: return run_attn_tc_d<T, FMT, 32, CAUSAL>(k, p, a, c, dt);
+    case 64: return run_attn_tc_d<T, FMT, 64, CAUSAL>(k, p, a, c, dt);
+    case 128: return run_attn_tc_d<T, FMT, 128, CAUSAL>(k, p, a, c, dt);
+    default: return GPO_INTERNAL;
+  }
+}
+
+gpo_status launch_attention_tc(const gpo_key& k, const Plan& p, const gpo_args& a,
+                               const LaunchCtx& c) {
+  if (!a.in[0] || !a.in[1] || !a.in[2] || !a.out) return GPO_BAD_ARGS;
+  if (!aligned16(a.in[0]) || !aligned16(a.in[1]) || !aligned16(a.in[2]) || !aligned16(a.out))
+    return GPO_BAD_ARGS;
+  if (k.shape[0] == 0 || k.shape[1] == 0) return GPO_OK;
+  const bool causal = k.task == GPO_TASK_ATTENTION_CAUSAL;
+  if (k.dtype == GPO_BFLOAT16)
+    return causal ? run_attn_tc_bn<__nv_bfloat16, 1, true>(k, p, a, c,
+                                                           CU_TENSOR_MAP_DATA_TYPE_BFLOAT16)
+                  : run_attn_tc_bn<__nv_bfloat16, 1, false>(k, p, a, c,
+                                                            CU_TENSOR_MAP_DATA_TYPE_BFLOAT16);
+  if (k.dtype == GPO_FLOAT16)
+    return causal ? run_attn_tc_bn<__half, 0, true>(k, p, a, c, CU_TENSOR_MAP_DATA_TYPE_FLOAT16)
+                  : run_attn_tc_bn<__half, 0, false>(k, p, a, c, CU_TENSOR_MAP_DATA_TYPE_FLOAT16);
+  return GPO_BAD_ARGS;
+}
+
+}  // namespace gpo

@@ -1,0 +1,435 @@
+// C = A @ B on the 5th-generation tensor cores (tcgen05) for sm_100a.
+//
+// Replaces matmul_kernel (compiler/triton/kernels.py:26-65) for 16-bit and
+// tf32 candidates whose BLOCK_M is 128 or 256.  A is M x K row-major
+// (K-major operand), B is K x N row-major (MN-major operand, the layout the
+// reference passes: runner.py:107 stride_bk = N), C is M x N in A's dtype
+// (runner.py:101), fp32 accumulation in TMEM.
+//
+// Config mapping (one instantiation per (dtype, BLOCK_M, BLOCK_N, warps)):
+//   BLOCK_M    : 128 -> one M=128 MMA per K step; 256 -> two M=128 MMAs into
+//                two TMEM accumulators sharing the B tile.
+//   BLOCK_N    : MMA N and TMEM columns per accumulator.
+//   BLOCK_K    : K extent of one TMA stage (runtime); the MMA issuer walks it
+//                in 32-byte K steps (16 bf16/fp16 or 8 tf32 elements).
+//   num_stages : depth of the TMA -> MMA shared-memory ring (runtime).
+//   GROUP_M    : grouped tile raster for L2 reuse (runtime), as the
+//                reference's program-id swizzle (kernels.py:38-46).
+//   num_warps  : 4 -> one output tile per CTA; warp 0 lane 0 issues TMA,
+//                warp 1 lane 0 issues MMA, then all 4 warps drain TMEM.
+//                8 -> persistent CTA per SM, warp-specialised: warp 0 TMA,
+//                warp 1 MMA, warp 2 TMEM owner, warps 4-7 epilogue, with two
+//                TMEM accumulator buffers so the epilogue of tile i overlaps
+//                the main loop of tile i+1.
+//
+// Shared-memory operand layouts are the canonical UMMA layouts written by
+// TMA with hardware swizzle: A as K-atoms of BLOCK_M rows x S_A bytes
+// (S_A = min(BLOCK_K*es, 128)), B as N-chunks of BLOCK_K rows x S_B bytes
+// (S_B = min(BLOCK_N*es, 128)).  Out-of-bounds rows / columns of partial
+// tiles are zero-filled by TMA, so ragged M, N and K need no special path;
+// the epilogue masks the stores.
+#include <algorithm>
+#include <mutex>
+
+#include "gpo_common.cuh"
+#include "gpo_internal.h"
+
+namespace gpo {
+
+constexpr int kMaxStages = 8;
+
+struct TcShared {
+  uint64_t full[kMaxStages];
+  uint64_t empty[kMaxStages];
+  uint64_t acc_full[2];
+  uint64_t acc_empty[2];
+  uint64_t drain;
+  uint32_t tmem_base;
+  int abort;
+};
+
+__device__ __forceinline__ void tile_coords(int tile, int num_pid_m, int num_pid_n, int group_m,
+                                            int& pm, int& pn) {
+  const int in_group = group_m * num_pid_n;
+  const int gid = tile / in_group;
+  const int first_m = gid * group_m;
+  const int gsize = min(num_pid_m - first_m, group_m);
+  pm = first_m + (tile % gsize);
+  pn = (tile % in_group) / gsize;
+}
+
+template <typename T, int FMT, int BM, int BN, bool PERSISTENT>
+__global__ void __launch_bounds__(PERSISTENT ? 256 : 128, 1)
+    matmul_tc_kernel(const __grid_constant__ CUtensorMap tma_a,
+                     const __grid_constant__ CUtensorMap tma_b, T* __restrict__ C, int M, int N,
+                     int K, int BK, int stages, int group_m, int swa, unsigned int* err) {
+  constexpr int ES = sizeof(T);
+  constexpr int SWB = (BN * ES) < 128 ? (BN * ES) : 128;
+  constexpr int HALVES = BM / 128;
+  constexpr int COLS = HALVES * BN;  // TMEM columns per accumulator buffer
+  constexpr int ACC_STAGES = (PERSISTENT && 2 * COLS <= 512) ? 2 : 1;
+  constexpr int ALLOC = (ACC_STAGES * COLS) <= 32    ? 32
+                        : (ACC_STAGES * COLS) <= 64  ? 64
+                        : (ACC_STAGES * COLS) <= 128 ? 128
+                        : (ACC_STAGES * COLS) <= 256 ? 256
+                                                     : 512;
+  constexpr int KSTEP = 32 / ES;  // K elements per MMA instruction
+  constexpr uint32_t IDESC = make_idesc(FMT, 128, BN, false, true);
+
+  __shared__ TcShared sh;
+  extern __shared__ uint8_t dyn_smem[];
+  const uint32_t smem_base = (smem_u32(dyn_smem) + 1023u) & ~1023u;
+  const uint32_t a_bytes = static_cast<uint32_t>(BM) * BK * ES;
+  const uint32_t b_bytes = static_cast<uint32_t>(BK) * BN * ES;
+  const uint32_t stage_bytes = (a_bytes + b_bytes + 1023u) & ~1023u;
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int num_pid_m = (M + BM - 1) / BM;
+  const int num_pid_n = (N + BN - 1) / BN;
+  const int num_tiles = num_pid_m * num_pid_n;
+  const int num_kb = (K + BK - 1) / BK;
+  const int tile_step = PERSISTENT ? gridDim.x : num_tiles;
+  const int alloc_warp = PERSISTENT ? 2 : 0;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < stages; ++s) {
+      mbar_init(smem_u32(&sh.full[s]), 1);
+      mbar_init(smem_u32(&sh.empty[s]), 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(smem_u32(&sh.acc_full[b]), 1);
+      mbar_init(smem_u32(&sh.acc_empty[b]), 4);
+    }
+    mbar_init(smem_u32(&sh.drain), 1);
+    sh.abort = 0;
+    fence_barrier_init();
+    tma_prefetch_desc(&tma_a);
+    tma_prefetch_desc(&tma_b);
+  }
+  if (warp == alloc_warp) {
+    tmem_alloc(smem_u32(&sh.tmem_base), ALLOC);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = sh.tmem_base;
+  volatile int* abort_flag = &sh.abort;
+
+  // ------------------------------------------------------------ producer
+  if (warp == 0 && lane == 0) {
+    int it = 0;
+    bool ok = true;
+    for (int tile = blockIdx.x; tile < num_tiles && ok; tile += tile_step) {
+      int pm, pn;
+      tile_coords(tile, num_pid_m, num_pid_n, group_m, pm, pn);
+      for (int kb = 0; kb < num_kb; ++kb, ++it) {
+        const int s = it % stages;
+        const uint32_t r = static_cast<uint32_t>(it / stages);
+        if (!mbar_wait(smem_u32(&sh.empty[s]), (r & 1u) ^ 1u, abort_flag, err,
+                       kErrWaitProducer)) {
+          ok = false;
+          break;
+        }
+        const uint32_t full = smem_u32(&sh.full[s]);
+        mbar_arrive_expect_tx(full, a_bytes + b_bytes);
+        const uint32_t sa = smem_base + s * stage_bytes;
+        const uint32_t sb = sa + a_bytes;
+        const int a_atoms = (BK * ES) / swa;
+        for (int a = 0; a < a_atoms; ++a)
+          tma_load_2d(sa + a * BM * swa, &tma_a, full, kb * BK + a * (swa / ES), pm * BM);
+#pragma unroll
+        for (int c = 0; c < (BN * ES) / SWB; ++c)
+          tma_load_2d(sb + c * BK * SWB, &tma_b, full, pn * BN + c * (SWB / ES), kb * BK);
+      }
+    }
+    if (!ok) {
+      // drain every load still in flight before the CTA may exit
+      for (int j = max(0, it - stages); j < it; ++j)
+        mbar_wait_drain(smem_u32(&sh.full[j % stages]), static_cast<uint32_t>(j / stages) & 1u,
+                        err);
+    }
+  }
+  // ---------------------------------------------------------- MMA issuer
+  else if (warp == 1 && lane == 0) {
+    int it = 0, tcount = 0;
+    bool ok = true;
+    for (int tile = blockIdx.x; tile < num_tiles && ok; tile += tile_step, ++tcount) {
+      const int buf = tcount % ACC_STAGES;
+      const uint32_t use = static_cast<uint32_t>(tcount / ACC_STAGES);
+      if (PERSISTENT) {
+        if (!mbar_wait(smem_u32(&sh.acc_empty[buf]), (use & 1u) ^ 1u, abort_flag, err,
+                       kErrWaitMma)) {
+          ok = false;
+          break;
+        }
+      }
+      tc_fence_after();
+      const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(buf * COLS);
+      for (int kb = 0; kb < num_kb; ++kb, ++it) {
+        const int s = it % stages;
+        const uint32_t r = static_cast<uint32_t>(it / stages);
+        if (!mbar_wait(smem_u32(&sh.full[s]), r & 1u, abort_flag, err, kErrWaitMma)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t sa = smem_base + s * stage_bytes;
+        const uint32_t sb = sa + a_bytes;
+        const int ksteps = BK / KSTEP;
+        for (int kk = 0; kk < ksteps; ++kk) {
+          const uint32_t kbyte = static_cast<uint32_t>(kk) * 32u;
+          const uint32_t a_off = (kbyte / swa) * (BM * swa) + (kbyte % swa);
+          const uint64_t bdesc =
+              make_smem_desc(sb + kk * KSTEP * SWB, BK * SWB, 8 * SWB, SWB);
+#pragma unroll
+          for (int h = 0; h < HALVES; ++h) {
+            const uint64_t adesc = make_smem_desc(sa + a_off + h * 128 * swa, 16, 8 * swa, swa);
+            const uint32_t acc = (kb | kk) != 0 ? 1u : 0u;
+            if constexpr (FMT == 2)
+              mma_tf32_ss(d_tmem + h * BN, adesc, bdesc, IDESC, acc);
+            else
+              mma_f16_ss(d_tmem + h * BN, adesc, bdesc, IDESC, acc);
+          }
+        }
+        mma_commit(smem_u32(&sh.empty[s]));  // stage reusable once these MMAs finish
+      }
+      if (!ok) break;
+      mma_commit(smem_u32(&sh.acc_full[buf]));
+    }
+    if (!ok) {
+      mma_commit(smem_u32(&sh.drain));
+      mbar_wait_drain(smem_u32(&sh.drain), 0, err);
+    }
+  }
+
+  // ------------------------------------------------------------ epilogue
+  const bool epi_warp = PERSISTENT ? (warp >= 4) : true;
+  if (epi_warp) {
+    __syncwarp();
+    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    int tcount = 0;
+    for (int tile = blockIdx.x; tile < num_tiles; tile += tile_step, ++tcount) {
+      const int buf = tcount % ACC_STAGES;
+      const uint32_t use = static_cast<uint32_t>(tcount / ACC_STAGES);
+      if (!mbar_wait(smem_u32(&sh.acc_full[buf]), use & 1u, abort_flag, err, kErrWaitEpilogue))
+        break;
+      tc_fence_after();
+      int pm, pn;
+      tile_coords(tile, num_pid_m, num_pid_n, group_m, pm, pn);
+#pragma unroll
+      for (int h = 0; h < HALVES; ++h) {
+        const int row = pm * BM + h * 128 + q * 32 + lane;
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; ++c) {
+          uint32_t r[32];
+          tmem_ld32(tmem_base + (static_cast<uint32_t>(q * 32) << 16) +
+                        static_cast<uint32_t>(buf * COLS + h * BN + c * 32),
+                    r);
+          tmem_wait_ld();
+          const int col0 = pn * BN + c * 32;
+          if (row < M) {
+            T* dst = C + static_cast<int64_t>(row) * N + col0;
+            if (col0 + 32 <= N) {
+              if constexpr (ES == 2) {
+                uint32_t pk[16];
+#pragma unroll
+                for (int i = 0; i < 16; ++i) {
+                  const float lo = __uint_as_float(r[2 * i]), hi = __uint_as_float(r[2 * i + 1]);
+                  pk[i] = (FMT == 1) ? pack_bf16(lo, hi) : pack_f16(lo, hi);
+                }
+                uint4* d4 = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+                for (int i = 0; i < 4; ++i)
+                  d4[i] = make_uint4(pk[4 * i], pk[4 * i + 1], pk[4 * i + 2], pk[4 * i + 3]);
+              } else {
+                uint4* d4 = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+                for (int i = 0; i < 8; ++i)
+                  d4[i] = make_uint4(r[4 * i], r[4 * i + 1], r[4 * i + 2], r[4 * i + 3]);
+              }
+            } else {
+#pragma unroll
+              for (int i = 0; i < 32; ++i)
+                if (col0 + i < N) dst[i] = Elem<T>::from_f(__uint_as_float(r[i]));
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_u32(&sh.acc_empty[buf]));
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == alloc_warp) tmem_dealloc(tmem_base, ALLOC);
+}
+
+// ------------------------------------------------------------------- host
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                  const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                  const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static CUtensorMapSwizzle swizzle_enum(int bytes) {
+  return bytes == 128 ? CU_TENSOR_MAP_SWIZZLE_128B
+         : bytes == 64 ? CU_TENSOR_MAP_SWIZZLE_64B
+                       : CU_TENSOR_MAP_SWIZZLE_32B;
+}
+
+// 2-D row-major tensor [rows, cols] (cols contiguous) with box
+// [box_rows, box_cols].
+static bool encode_2d(CUtensorMap* map, CUtensorMapDataType dt, const void* ptr, uint64_t rows,
+                      uint64_t cols, int es, uint32_t box_cols, uint32_t box_rows, int swz) {
+  EncodeTiledFn fn = reinterpret_cast<EncodeTiledFn>(tensor_map_encoder());
+  if (!fn) return false;
+  const cuuint64_t dims[2] = {cols, rows};
+  const cuuint64_t strides[1] = {cols * static_cast<uint64_t>(es)};
+  const cuuint32_t box[2] = {box_cols, box_rows};
+  const cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, dt, 2, const_cast<void*>(ptr), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle_enum(swz),
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+// Plan: aux[0] = swizzle bytes of A, aux[1] = dynamic smem bytes,
+// aux[2] = persistent flag.
+gpo_status plan_matmul_tc(const gpo_key& k, Plan& p, std::string& log) {
+  const int es = dtype_bytes(k.dtype);
+  const int BM = k.block_m, BN = k.block_n, BK = k.block_k;
+  const int64_t M = k.shape[0], N = k.shape[1], K = k.shape[2];
+  if (BM != 128 && BM != 256) {
+    log = "tcgen05 family needs BLOCK_M 128 or 256";
+    return GPO_BAD_CONFIG;
+  }
+  if (BN != 32 && BN != 64 && BN != 128 && BN != 256) {
+    log = "tcgen05 family needs BLOCK_N in {32, 64, 128, 256}";
+    return GPO_BAD_CONFIG;
+  }
+  if (BK < 1 || (BK & (BK - 1)) || BK * es < 32 || BK > 256) {
+    log = "tcgen05 family needs BLOCK_K a power of two with BLOCK_K*es >= 32 and <= 256";
+    return GPO_BAD_CONFIG;
+  }
+  if (k.num_warps != 4 && k.num_warps != 8) {
+    log = "tcgen05 family needs num_warps 4 or 8";
+    return GPO_BAD_CONFIG;
+  }
+  if ((K * es) % 16 || (N * es) % 16) {
+    log = "TMA needs K*es and N*es multiples of 16 bytes";
+    return GPO_BAD_CONFIG;
+  }
+  if (k.num_stages < 1 || k.num_stages > kMaxStages) {
+    log = "num_stages must be in [1, 8]";
+    return GPO_BAD_CONFIG;
+  }
+  if (k.group_m < 1) {
+    log = "GROUP_M must be >= 1";
+    return GPO_BAD_CONFIG;
+  }
+  const bool persistent = k.num_warps == 8;
+  const uint32_t a_bytes = static_cast<uint32_t>(BM) * BK * es;
+  const uint32_t b_bytes = static_cast<uint32_t>(BK) * BN * es;
+  const uint32_t stage = (a_bytes + b_bytes + 1023u) & ~1023u;
+  const uint32_t dyn = stage * static_cast<uint32_t>(k.num_stages) + 1024u;
+  const uint32_t smem = dyn + static_cast<uint32_t>(sizeof(TcShared));
+  const int cols = (BM / 128) * BN;
+  const int acc_stages = (persistent && 2 * cols <= 512) ? 2 : 1;
+  int alloc = 32;
+  while (alloc < acc_stages * cols) alloc *= 2;
+  if (smem > kMaxSmemPerCta) {
+    log = "shared memory " + std::to_string(smem) + " B (" + std::to_string(k.num_stages) +
+          " stages x " + std::to_string(stage) + " B) exceeds the 232448 B per-CTA limit";
+    return GPO_COMPILE_ERROR;
+  }
+  if (alloc > static_cast<int>(kTmemCols)) {
+    log = "TMEM accumulator needs " + std::to_string(alloc) + " columns > 512";
+    return GPO_COMPILE_ERROR;
+  }
+  p.aux[0] = std::min(BK * es, 128);
+  p.aux[1] = static_cast<int>(dyn);
+  p.aux[2] = persistent ? 1 : 0;
+  p.family = "matmul_tc";
+  p.res.smem_bytes = smem;
+  p.res.tmem_cols = static_cast<uint32_t>(alloc);
+  p.res.threads_per_cta = persistent ? 256u : 128u;
+  const uint64_t tiles = cdiv(M, BM) * cdiv(N, BN);
+  p.res.grid_x = static_cast<uint32_t>(tiles);  // persistent: clamped to the SM count at launch
+  p.res.grid_y = p.res.grid_z = 1;
+  p.res.persistent = persistent ? 1u : 0u;
+  p.res.launches_per_call = 1;
+  const char* tn = k.dtype == GPO_BFLOAT16 ? "bf16" : k.dtype == GPO_FLOAT16 ? "f16" : "tf32";
+  snprintf(p.res.kernel, sizeof(p.res.kernel), "matmul_tc_kernel<%s,%d,%d,%s>", tn, BM, BN,
+           persistent ? "persistent" : "tile");
+  return GPO_OK;
+}
+
+template <typename T, int FMT, int BM, int BN, bool P>
+static gpo_status run_tc(const gpo_key& k, const Plan& p, const gpo_args& a, const LaunchCtx& c,
+                         CUtensorMapDataType dt) {
+  const int es = sizeof(T);
+  const int64_t M = k.shape[0], N = k.shape[1], K = k.shape[2];
+  const int swa = p.aux[0];
+  constexpr int SWB = (BN * sizeof(T)) < 128 ? (BN * sizeof(T)) : 128;
+  CUtensorMap ma, mb;
+  if (!encode_2d(&ma, dt, a.in[0], M, K, es, swa / es, BM, swa)) return GPO_LAUNCH_ERROR;
+  if (!encode_2d(&mb, dt, a.in[1], K, N, es, SWB / es, k.block_k, SWB)) return GPO_LAUNCH_ERROR;
+  auto kern = matmul_tc_kernel<T, FMT, BM, BN, P>;
+  const uint32_t dyn = static_cast<uint32_t>(p.aux[1]);
+  gpo_status s = ensure_smem_attr(reinterpret_cast<const void*>(kern), dyn);
+  if (s != GPO_OK) return s;
+  const uint64_t tiles = cdiv(M, BM) * cdiv(N, BN);
+  const unsigned grid =
+      P ? static_cast<unsigned>(std::min<uint64_t>(tiles, c.sm_count)) : static_cast<unsigned>(tiles);
+  kern<<<grid, P ? 256 : 128, dyn, c.stream>>>(ma, mb, static_cast<T*>(a.out),
+                                               static_cast<int>(M), static_cast<int>(N),
+                                               static_cast<int>(K), k.block_k, k.num_stages,
+                                               k.group_m, swa, c.err);
+  return launch_status();
+}
+
+template <typename T, int FMT, int BM, bool P>
+static gpo_status run_tc_bn(const gpo_key& k, const Plan& p, const gpo_args& a,
+                            const LaunchCtx& c, CUtensorMapDataType dt) {
+  switch (k.block_n) {
+    case 32: return run_tc<T, FMT, BM, 32, P>(k, p, a, c, dt);
+    case 64: return run_tc<T, FMT, BM, 64, P>(k, p, a, c, dt);
+    case 128: return run_tc<T, FMT, BM, 128, P>(k, p, a, c, dt);
+    case 256: return run_tc<T, FMT, BM, 256, P>(k, p, a, c, dt);
+    default: return GPO_INTERNAL;
+  }
+}
+
+template <typename T, int FMT>
+static gpo_status run_tc_dt(const gpo_key& k, const Plan& p, const gpo_args& a,
+                            const LaunchCtx& c, CUtensorMapDataType dt) {
+  const bool P = p.aux[2] != 0;
+  if (k.block_m == 128)
+    return P ? run_tc_bn<T, FMT, 128, true>(k, p, a, c, dt)
+             : run_tc_bn<T, FMT, 128, false>(k, p, a, c, dt);
+  return P ? run_tc_bn<T, FMT, 256, true>(k, p, a, c, dt)
+           : run_tc_bn<T, FMT, 256, false>(k, p, a, c, dt);
+}
+
+gpo_status launch_matmul_tc(const gpo_key& k, const Plan& p, const gpo_args& a,
+                            const LaunchCtx& c) {
+  if (!a.in[0] || !a.in[1] || !a.out) return GPO_BAD_ARGS;
+  if (!aligned16(a.in[0]) || !aligned16(a.in[1]) || !aligned16(a.out)) return GPO_BAD_ARGS;
+  if (k.shape[0] == 0 || k.shape[1] == 0) return GPO_OK;
+  switch (k.dtype) {
+    case GPO_BFLOAT16:
+      return run_tc_dt<__nv_bfloat16, 1>(k, p, a, c, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16);
+    case GPO_FLOAT16:
+      return run_tc_dt<__half, 0>(k, p, a, c, CU_TENSOR_MAP_DATA_TYPE_FLOAT16);
+    case GPO_TF32:
+      return run_tc_dt<float, 2>(k, p, a, c, CU_TENSOR_MAP_DATA_TYPE_FLOAT32);
+    default:
+      return GPO_BAD_ARGS;
+  }
+}
+
+}  // namespace gpo

@@ -1,0 +1,487 @@
+// Row-wise kernel families: softmax and layernorm over the last dimension.
+//
+// One CTA of num_warps*32 threads per row (grid (M,), as
+// compiler/triton/runner.py:175,194 launch).  BLOCK_N selects the strategy
+// exactly as the reference does (runner.py:170,189):
+//   BLOCK_N >= N : single tile — the row is read from HBM once, held in
+//                  registers (or, when the per-thread share exceeds 64
+//                  values, staged in shared memory), reduced, and written.
+//   BLOCK_N <  N : online / two-pass — statistics pass over BLOCK_N tiles,
+//                  then a normalise pass that re-reads the row (which on
+//                  B200 mostly hits the 126 MB L2).
+// Thread t owns V consecutive elements (one 16-byte vector) per vector slot
+// and slots are strided by the CTA width, so every warp access is a
+// contiguous 512-byte segment.  Statistics are fp32.
+#include <algorithm>
+
+#include "gpo_common.cuh"
+#include "gpo_internal.h"
+
+namespace gpo {
+
+template <typename T>
+struct RowVec {
+  static constexpr int V = 16 / sizeof(T);
+};
+
+// Load vector slot j (V consecutive elements) of tile [tile0, tile0+bn)
+// owned by this thread; out-of-range elements read as `fill`.
+template <typename T>
+__device__ __forceinline__ void row_load_slot(const T* __restrict__ row, int64_t n, int64_t tile0,
+                                              int64_t bn, bool vec, float fill, int j,
+                                              float* x) {
+  using E = Elem<T>;
+  constexpr int V = RowVec<T>::V;
+  const int64_t vi = threadIdx.x + static_cast<int64_t>(j) * blockDim.x;
+  const int64_t e0 = tile0 + vi * V;
+  const bool in_tile = vi * V < bn;
+  if (vec && in_tile && e0 + V <= n) {
+    uint4 r = __ldcs(reinterpret_cast<const uint4*>(row + e0));
+    const T* er = reinterpret_cast<const T*>(&r);
+#pragma unroll
+    for (int u = 0; u < V; ++u) x[u] = E::to_f(er[u]);
+  } else {
+#pragma unroll
+    for (int u = 0; u < V; ++u) {
+      const int64_t e = e0 + u;
+      x[u] = (in_tile && vi * V + u < bn && e < n) ? E::to_f(row[e]) : fill;
+    }
+  }
+}
+
+// Load the VPT vector slots of tile [tile0, tile0+bn) owned by this thread.
+template <typename T, int VPT>
+__device__ __forceinline__ void row_load(const T* __restrict__ row, int64_t n, int64_t tile0,
+                                         int64_t bn, bool vec, float fill,
+                                         float (&x)[VPT * RowVec<T>::V]) {
+#pragma unroll
+  for (int j = 0; j < VPT; ++j) row_load_slot<T>(row, n, tile0, bn, vec, fill, j, x + j * RowVec<T>::V);
+}
+
+// y = (x - mean) * rstd * w + b over this thread's slots of one tile.
+template <typename T, int VPT>
+__device__ __forceinline__ void ln_affine(const T* __restrict__ w, const T* __restrict__ b,
+                                          int64_t n, int64_t tile0, int64_t bn, bool vec,
+                                          float mean, float rstd,
+                                          float (&v)[VPT * RowVec<T>::V]) {
+  constexpr int V = RowVec<T>::V;
+#pragma unroll
+  for (int j = 0; j < VPT; ++j) {
+    float wv[V], bv[V];
+    row_load_slot<T>(w, n, tile0, bn, vec, 0.f, j, wv);
+    row_load_slot<T>(b, n, tile0, bn, vec, 0.f, j, bv);
+#pragma unroll
+    for (int u = 0; u < V; ++u) v[j * V + u] = (v[j * V + u] - mean) * rstd * wv[u] + bv[u];
+  }
+}
+
+template <typename T, int VPT>
+__device__ __forceinline__ void row_store(T* __restrict__ row, int64_t n, int64_t tile0,
+                                          int64_t bn, bool vec,
+                                          const float (&y)[VPT * RowVec<T>::V]) {
+  using E = Elem<T>;
+  constexpr int V = RowVec<T>::V;
+#pragma unroll
+  for (int j = 0; j < VPT; ++j) {
+    const int64_t vi = threadIdx.x + static_cast<int64_t>(j) * blockDim.x;
+    const int64_t e0 = tile0 + vi * V;
+    const bool in_tile = vi * V < bn;
+    if (vec && in_tile && e0 + V <= n) {
+      uint4 r;
+      T* er = reinterpret_cast<T*>(&r);
+#pragma unroll
+      for (int u = 0; u < V; ++u) er[u] = E::from_f(y[j * V + u]);
+      __stcs(reinterpret_cast<uint4*>(row + e0), r);
+    } else {
+#pragma unroll
+      for (int u = 0; u < V; ++u) {
+        const int64_t e = e0 + u;
+        if (in_tile && vi * V + u < bn && e < n) row[e] = E::from_f(y[j * V + u]);
+      }
+    }
+  }
+}
+
+// Block reductions; every thread receives the result.
+__device__ __forceinline__ float block_allreduce_max(float v, float* red) {
+  v = warp_max(v);
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31, nw = blockDim.x >> 5;
+  __syncthreads();
+  if (l == 0) red[w] = v;
+  __syncthreads();
+  float r = l < nw ? red[l] : -INFINITY;
+  return warp_max(r);
+}
+__device__ __forceinline__ float block_allreduce_sum(float v, float* red) {
+  v = warp_sum(v);
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31, nw = blockDim.x >> 5;
+  __syncthreads();
+  if (l == 0) red[w] = v;
+  __syncthreads();
+  float r = l < nw ? red[l] : 0.f;
+  return warp_sum(r);
+}
+
+// ---------------------------------------------------------------- softmax
+// Single tile held in registers (softmax_kernel SINGLE_TILE branch,
+// compiler/triton/kernels.py:113-120).
+template <typename T, int VPT>
+__global__ void __launch_bounds__(1024) softmax_tile_regs(const T* __restrict__ x,
+                                                          T* __restrict__ y, int64_t n,
+                                                          int64_t bn, int vec) {
+  constexpr int V = RowVec<T>::V;
+  __shared__ float red[32];
+  const T* xr = x + static_cast<int64_t>(blockIdx.x) * n;
+  T* yr = y + static_cast<int64_t>(blockIdx.x) * n;
+  float v[VPT * V];
+  row_load<T, VPT>(xr, n, 0, bn, vec, -INFINITY, v);
+  float m = -INFINITY;
+#pragma unroll
+  for (int i = 0; i < VPT * V; ++i) m = fmaxf(m, v[i]);
+  m = block_allreduce_max(m, red);
+  float s = 0.f;
+#pragma unroll
+  for (int i = 0; i < VPT * V; ++i) {
+    v[i] = expf(v[i] - m);  // exp(-inf) = 0 for masked slots
+    s += v[i];
+  }
+  s = block_allreduce_sum(s, red);
+#pragma unroll
+  for (int i = 0; i < VPT * V; ++i) v[i] = v[i] / s;
+  row_store<T, VPT>(yr, n, 0, bn, vec, v);
+}
+
+// Single tile staged in shared memory (fp32 copy of the row) when the
+// per-thread share is too large for registers.
+template <typename T>
+__global__ void __launch_bounds__(1024) softmax_tile_smem(const T* __restrict__ x,
+                                                          T* __restrict__ y, int64_t n) {
+  using E = Elem<T>;
+  extern __shared__ float srow[];
+  __shared__ float red[32];
+  const T* xr = x + static_cast<int64_t>(blockIdx.x) * n;
+  T* yr = y + static_cast<int64_t>(blockIdx.x) * n;
+  float m = -INFINITY;
+  for (int64_t i = threadIdx.x; i < n; i += blockDim.x) {
+    const float f = E::to_f(xr[i]);
+    srow[i] = f;
+    m = fmaxf(m, f);
+  }
+  m = block_allreduce_max(m, red);
+  float s = 0.f;
+  for (int64_t i = threadIdx.x; i < n; i += blockDim.x) {
+    const float e = expf(srow[i] - m);
+    srow[i] = e;
+    s += e;
+  }
+  s = block_allreduce_sum(s, red);
+  for (int64_t i = threadIdx.x; i < n; i += blockDim.x) yr[i] = E::from_f(srow[i] / s);
+}
+
+// Online two-pass softmax over BLOCK_N tiles (kernels.py:121-136): running
+// (max, sum) per thread merged across the CTA, then a normalise pass.
+template <typename T, int VPT>
+__global__ void __launch_bounds__(1024) softmax_online(const T* __restrict__ x,
+                                                       T* __restrict__ y, int64_t n, int64_t bn,
+                                                       int vec) {
+  constexpr int V = RowVec<T>::V;
+  __shared__ float red[32];
+  const T* xr = x + static_cast<int64_t>(blockIdx.x) * n;
+  T* yr = y + static_cast<int64_t>(blockIdx.x) * n;
+  float m = -INFINITY, s = 0.f;
+  float v[VPT * V];
+  for (int64_t t0 = 0; t0 < n; t0 += bn) {
+    row_load<T, VPT>(xr, n, t0, bn, vec, -INFINITY, v);
+    float tm = -INFINITY;
+#pragma unroll
+    for (int i = 0; i < VPT * V; ++i) tm = fmaxf(tm, v[i]);
+    const float nm = fmaxf(m, tm);
+    if (nm != -INFINITY) {
+      float ts = 0.f;
+#pragma unroll
+      for (int i = 0; i < VPT * V; ++i) ts += expf(v[i] - nm);
+      s = s * expf(m - nm) + ts;
+      m = nm;
+    }
+  }
+  const float M = block_allreduce_max(m, red);
+  const float S = block_allreduce_sum(m == -INFINITY ? 0.f : s * expf(m - M), red);
+  for (int64_t t0 = 0; t0 < n; t0 += bn) {
+    row_load<T, VPT>(xr, n, t0, bn, vec, -INFINITY, v);
+#pragma unroll
+    for (int i = 0; i < VPT * V; ++i) v[i] = expf(v[i] - M) / S;
+    row_store<T, VPT>(yr, n, t0, bn, vec, v);
+  }
+}
+
+// -------------------------------------------------------------- layernorm
+// Single tile, centred variance (layernorm_kernel SINGLE_TILE branch,
+// kernels.py:148-159).
+template <typename T, int VPT>
+__global__ void __launch_bounds__(1024) layernorm_tile_regs(const T* __restrict__ x,
+                                                            const T* __restrict__ w,
+                                                            const T* __restrict__ b,
+                                                            T* __restrict__ y, int64_t n,
+                                                            int64_t bn, float eps, int vec) {
+  constexpr int V = RowVec<T>::V;
+  __shared__ float red[32];
+  const T* xr = x + static_cast<int64_t>(blockIdx.x) * n;
+  T* yr = y + static_cast<int64_t>(blockIdx.x) * n;
+  float v[VPT * V];
+  row_load<T, VPT>(xr, n, 0, bn, vec, 0.f, v);
+  float s = 0.f;
+#pragma unroll
+  for (int i = 0; i < VPT * V; ++i) s += v[i];
+  const float mean = block_allreduce_sum(s, red) / static_cast<float>(n);
+  float q = 0.f;
+#pragma unroll
+  for (int j = 0; j < VPT; ++j) {
+    const int64_t e0 = (threadIdx.x + static_cast<int64_t>(j) * blockDim.x) * V;
+#pragma unroll
+    for (int u = 0; u < V; ++u) {
+      const float d = (e0 + u < n) ? v[j * V + u] - mean : 0.f;
+      q += d * d;
+    }
+  }
+  const float var = block_allreduce_sum(q, red) / static_cast<float>(n);
+  const float rstd = 1.0f / sqrtf(var + eps);
+  ln_affine<T, VPT>(w, b, n, 0, bn, vec, mean, rstd, v);
+  row_store<T, VPT>(yr, n, 0, bn, vec, v);
+}
+
+template <typename T>
+__global__ void __launch_bounds__(1024) layernorm_tile_smem(const T* __restrict__ x,
+                                                            const T* __restrict__ w,
+                                                            const T* __restrict__ b,
+                                                            T* __restrict__ y, int64_t n,
+                                                            float eps) {
+  using E = Elem<T>;
+  extern __shared__ float srow[];
+  __shared__ float red[32];
+  const T* xr = x + static_cast<int64_t>(blockIdx.x) * n;
+  T* yr = y + static_cast<int64_t>(blockIdx.x) * n;
+  float s = 0.f;
+  for (int64_t i = threadIdx.x; i < n; i += blockDim.x) {
+    const float f = E::to_f(xr[i]);
+    srow[i] = f;
+    s += f;
+  }
+  const float mean = block_allreduce_sum(s, red) / static_cast<float>(n);
+  float q = 0.f;
+  for (int64_t i = threadIdx.x; i < n; i += blockDim.x) {
+    const float d = srow[i] - mean;
+    q += d * d;
+  }
+  const float var = block_allreduce_sum(q, red) / static_cast<float>(n);
+  const float rstd = 1.0f / sqrtf(var + eps);
+  for (int64_t i = threadIdx.x; i < n; i += blockDim.x)
+    yr[i] = E::from_f((srow[i] - mean) * rstd * E::to_f(w[i]) + E::to_f(b[i]));
+}
+
+// Tiled two-pass layernorm with var = E[x^2] - E[x]^2 clamped at 0
+// (kernels.py:160-179).
+template <typename T, int VPT>
+__global__ void __launch_bounds__(1024) layernorm_twopass(const T* __restrict__ x,
+                                                          const T* __restrict__ w,
+                                                          const T* __restrict__ b,
+                                                          T* __restrict__ y, int64_t n,
+                                                          int64_t bn, float eps, int vec) {
+  constexpr int V = RowVec<T>::V;
+  __shared__ float red[32];
+  const T* xr = x + static_cast<int64_t>(blockIdx.x) * n;
+  T* yr = y + static_cast<int64_t>(blockIdx.x) * n;
+  float v[VPT * V];
+  float s = 0.f, q = 0.f;
+  for (int64_t t0 = 0; t0 < n; t0 += bn) {
+    row_load<T, VPT>(xr, n, t0, bn, vec, 0.f, v);
+#pragma unroll
+    for (int i = 0; i < VPT * V; ++i) {
+      s += v[i];
+      q += v[i] * v[i];
+    }
+  }
+  const float total = block_allreduce_sum(s, red);
+  const float total_sq = block_allreduce_sum(q, red);
+  const float mean = total / static_cast<float>(n);
+  const float var = fmaxf(total_sq / static_cast<float>(n) - mean * mean, 0.f);
+  const float rstd = 1.0f / sqrtf(var + eps);
+  for (int64_t t0 = 0; t0 < n; t0 += bn) {
+    row_load<T, VPT>(xr, n, t0, bn, vec, 0.f, v);
+    ln_affine<T, VPT>(w, b, n, t0, bn, vec, mean, rstd, v);
+    row_store<T, VPT>(yr, n, t0, bn, vec, v);
+  }
+}
+
+// ------------------------------------------------------------------- host
+// Plan: aux[0] = VPT (vector slots per thread, 0 = smem-staged single tile),
+// aux[1] = single-tile flag, aux[2] = dynamic smem bytes.
+static gpo_status plan_rows(const gpo_key& k, Plan& p, std::string& log, const char* what) {
+  if (k.ndim != 2 || k.shape[0] < 0 || k.shape[1] < 1) {
+    log = "expected a 2-D shape (M, N) with N >= 1";
+    return GPO_BAD_CONFIG;
+  }
+  if (k.dtype == GPO_TF32) {
+    log = "row kernels have no tf32 variant";
+    return GPO_BAD_CONFIG;
+  }
+  if (k.num_warps < 1 || k.num_warps > 32 || k.block_n < 1 || k.block_n > (1 << 16)) {
+    log = "num_warps must be in [1, 32] and BLOCK_N in [1, 65536]";
+    return GPO_BAD_CONFIG;
+  }
+  const int64_t n = k.shape[1];
+  const int threads = k.num_warps * 32;
+  const int V = 16 / dtype_bytes(k.dtype);
+  const bool single = k.block_n >= n;
+  const int64_t slots = static_cast<int64_t>(cdiv(k.block_n, static_cast<uint64_t>(threads) * V));
+  int vpt = 1;
+  while (vpt < slots) vpt *= 2;
+  const int vpt_max = 64 / V;  // at most 64 fp32 values per thread in registers
+  uint32_t dyn = 0;
+  if (vpt > vpt_max) {
+    if (!single) {
+      // tiles larger than the register budget cannot be processed in one
+      // sweep per thread; Triton's equivalent spills.  Report honestly.
+      log = "BLOCK_N tile needs " + std::to_string(slots * V) +
+            " fp32 values per thread (> 64-register tile budget) in the tiled variant";
+      return GPO_COMPILE_ERROR;
+    }
+    vpt = 0;
+    dyn = static_cast<uint32_t>(n) * 4u;
+    if (dyn + 128 > kMaxSmemPerCta) {
+      log = "row of " + std::to_string(n) + " fp32 values exceeds 227 KB shared memory";
+      return GPO_COMPILE_ERROR;
+    }
+  }
+  p.aux[0] = vpt;
+  p.aux[1] = single ? 1 : 0;
+  p.aux[2] = static_cast<int>(dyn);
+  p.family = "row_kernels";
+  p.res.threads_per_cta = static_cast<uint32_t>(threads);
+  p.res.grid_x = static_cast<uint32_t>(std::max<int64_t>(1, k.shape[0]));
+  p.res.grid_y = p.res.grid_z = 1;
+  p.res.launches_per_call = 1;
+  p.res.smem_bytes = dyn + 128;
+  snprintf(p.res.kernel, sizeof(p.res.kernel), "%s_%s<vpt=%d>", what,
+           single ? (vpt ? "tile_regs" : "tile_smem") : (k.task == GPO_TASK_SOFTMAX ? "online" : "twopass"),
+           vpt);
+  return GPO_OK;
+}
+
+gpo_status plan_softmax(const gpo_key& k, Plan& p, std::string& log) {
+  return plan_rows(k, p, log, "softmax");
+}
+gpo_status plan_layernorm(const gpo_key& k, Plan& p, std::string& log) {
+  return plan_rows(k, p, log, "layernorm");
+}
+
+template <typename T, int VPT>
+static gpo_status softmax_vpt(const gpo_key& k, const Plan& p, const gpo_args& a,
+                              const LaunchCtx& c, int vec) {
+  const unsigned grid = static_cast<unsigned>(k.shape[0]);
+  const int threads = k.num_warps * 32;
+  const T* x = static_cast<const T*>(a.in[0]);
+  T* y = static_cast<T*>(a.out);
+  if (p.aux[1])
+    softmax_tile_regs<T, VPT><<<grid, threads, 0, c.stream>>>(x, y, k.shape[1], k.block_n, vec);
+  else
+    softmax_online<T, VPT><<<grid, threads, 0, c.stream>>>(x, y, k.shape[1], k.block_n, vec);
+  return launch_status();
+}
+
+template <typename T>
+static gpo_status softmax_dt(const gpo_key& k, const Plan& p, const gpo_args& a,
+                             const LaunchCtx& c) {
+  const int vec = (aligned16(a.in[0]) && aligned16(a.out) &&
+                   (k.shape[1] * static_cast<int64_t>(sizeof(T))) % 16 == 0)
+                      ? 1
+                      : 0;
+  switch (p.aux[0]) {
+    case 0: {
+      const uint32_t dyn = static_cast<uint32_t>(p.aux[2]);
+      gpo_status s = ensure_smem_attr(reinterpret_cast<const void*>(&softmax_tile_smem<T>), dyn);
+      if (s != GPO_OK) return s;
+      softmax_tile_smem<T><<<static_cast<unsigned>(k.shape[0]), k.num_warps * 32, dyn, c.stream>>>(
+          static_cast<const T*>(a.in[0]), static_cast<T*>(a.out), k.shape[1]);
+      return launch_status();
+    }
+    case 1: return softmax_vpt<T, 1>(k, p, a, c, vec);
+    case 2: return softmax_vpt<T, 2>(k, p, a, c, vec);
+    case 4: return softmax_vpt<T, 4>(k, p, a, c, vec);
+    case 8: return softmax_vpt<T, 8>(k, p, a, c, vec);
+    case 16: return softmax_vpt<T, 16>(k, p, a, c, vec);
+    default: return GPO_INTERNAL;
+  }
+}
+
+gpo_status launch_softmax(const gpo_key& k, const Plan& p, const gpo_args& a, const LaunchCtx& c) {
+  if (!a.in[0] || !a.out) return GPO_BAD_ARGS;
+  if (k.shape[0] == 0) return GPO_OK;
+  switch (k.dtype) {
+    case GPO_FLOAT32: return softmax_dt<float>(k, p, a, c);
+    case GPO_FLOAT16: return softmax_dt<__half>(k, p, a, c);
+    case GPO_BFLOAT16: return softmax_dt<__nv_bfloat16>(k, p, a, c);
+    default: return GPO_BAD_ARGS;
+  }
+}
+
+template <typename T, int VPT>
+static gpo_status layernorm_vpt(const gpo_key& k, const Plan& p, const gpo_args& a,
+                                const LaunchCtx& c, int vec, float eps) {
+  const unsigned grid = static_cast<unsigned>(k.shape[0]);
+  const int threads = k.num_warps * 32;
+  const T* x = static_cast<const T*>(a.in[0]);
+  const T* w = static_cast<const T*>(a.in[1]);
+  const T* b = static_cast<const T*>(a.in[2]);
+  T* y = static_cast<T*>(a.out);
+  if (p.aux[1])
+    layernorm_tile_regs<T, VPT>
+        <<<grid, threads, 0, c.stream>>>(x, w, b, y, k.shape[1], k.block_n, eps, vec);
+  else
+    layernorm_twopass<T, VPT>
+        <<<grid, threads, 0, c.stream>>>(x, w, b, y, k.shape[1], k.block_n, eps, vec);
+  return launch_status();
+}
+
+template <typename T>
+static gpo_status layernorm_dt(const gpo_key& k, const Plan& p, const gpo_args& a,
+                               const LaunchCtx& c) {
+  const float eps = a.eps > 0.f ? a.eps : 1e-5f;
+  const int vec = (aligned16(a.in[0]) && aligned16(a.in[1]) && aligned16(a.in[2]) &&
+                   aligned16(a.out) &&
+                   (k.shape[1] * static_cast<int64_t>(sizeof(T))) % 16 == 0)
+                      ? 1
+                      : 0;
+  switch (p.aux[0]) {
+    case 0: {
+      const uint32_t dyn = static_cast<uint32_t>(p.aux[2]);
+      gpo_status s =
+          ensure_smem_attr(reinterpret_cast<const void*>(&layernorm_tile_smem<T>), dyn);
+      if (s != GPO_OK) return s;
+      layernorm_tile_smem<T>
+          <<<static_cast<unsigned>(k.shape[0]), k.num_warps * 32, dyn, c.stream>>>(
+              static_cast<const T*>(a.in[0]), static_cast<const T*>(a.in[1]),
+              static_cast<const T*>(a.in[2]), static_cast<T*>(a.out), k.shape[1], eps);
+      return launch_status();
+    }
+    case 1: return layernorm_vpt<T, 1>(k, p, a, c, vec, eps);
+    case 2: return layernorm_vpt<T, 2>(k, p, a, c, vec, eps);
+    case 4: return layernorm_vpt<T, 4>(k, p, a, c, vec, eps);
+    case 8: return layernorm_vpt<T, 8>(k, p, a, c, vec, eps);
+    case 16: return layernorm_vpt<T, 16>(k, p, a, c, vec, eps);
+    default: return GPO_INTERNAL;
+  }
+}
+
+gpo_status launch_layernorm(const gpo_key& k, const Plan& p, const gpo_args& a,
+                            const LaunchCtx& c) {
+  if (!a.in[0] || !a.in[1] || !a.in[2] || !a.out) return GPO_BAD_ARGS;
+  if (k.shape[0] == 0) return GPO_OK;
+  switch (k.dtype) {
+    case GPO_FLOAT32: return layernorm_dt<float>(k, p, a, c);
+    case GPO_FLOAT16: return layernorm_dt<__half>(k, p, a, c);
+    case GPO_BFLOAT16: return layernorm_dt<__nv_bfloat16>(k, p, a, c);
+    default: return GPO_BAD_ARGS;
+  }
+}
+
+}  // namespace gpo

@@ -1,0 +1,134 @@
+"""The C-ABI library: loads, exports every declared symbol, and applies the
+compile-error semantics on the host (no GPU, no compute calls)."""
+
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+
+from gpu_optimizer_b200 import _lib
+from gpu_optimizer_b200.runner import KernelBuildError, compile_module, render_source
+
+HEADER = Path(__file__).resolve().parent.parent / "include" / "gpo.h"
+
+
+def declared_functions():
+    text = HEADER.read_text()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(gpo_[a-z_]+)\s*\(", text)))
+
+
+def test_library_loads_and_exports_every_declared_symbol():
+    lib = _lib.load()
+    names = declared_functions()
+    assert len(names) >= 9
+    for n in names:
+        assert hasattr(lib, n), n
+        assert n in _lib.SIGNATURES, f"{n} has no ctypes signature"
+    assert lib.gpo_abi_version() == _lib.ABI_VERSION
+    assert _lib.status_name(_lib.COMPILE_ERROR) == "GPO_COMPILE_ERROR"
+
+
+def test_struct_layouts_match_header():
+    # int32 x 11 (44 B) + pad to 8 + int64 x 4
+    assert ctypes.sizeof(_lib.GpoKey) == 48 + 32
+    assert ctypes.sizeof(_lib.GpoArgs) == 8 * 4 + 8 + 8 * 2 + 4 + 4
+
+
+def mm(cfg, shape=(4096, 4096, 4096)):
+    base = {"BLOCK_M": 128, "BLOCK_N": 256, "BLOCK_K": 64, "GROUP_M": 8, "num_warps": 8,
+            "num_stages": 4, "dtype": "bfloat16"}
+    return compile_module("matmul", shape, {**base, **cfg})
+
+
+def test_tcgen05_matmul_plan():
+    res = mm({}).resources()
+    assert res["kernel"].startswith("matmul_tc_kernel<bf16,128,256,persistent>")
+    assert res["tmem_cols"] == 512  # two 256-column accumulators (double buffer)
+    assert res["smem_bytes"] <= 227 * 1024
+    assert res["persistent"]
+    res4 = mm({"num_warps": 4}).resources()
+    assert res4["tmem_cols"] == 256 and not res4["persistent"]
+    assert res4["grid"][0] == 32 * 16
+
+
+def test_shared_memory_overflow_is_a_compile_error():
+    with pytest.raises(KernelBuildError) as ei:
+        mm({"BLOCK_M": 256, "BLOCK_N": 256, "BLOCK_K": 128, "num_stages": 6})
+    assert "GPO_COMPILE_ERROR" in str(ei.value) and "shared memory" in ei.value.log
+
+
+def test_simt_register_tile_overflow_is_a_compile_error():
+    with pytest.raises(KernelBuildError) as ei:
+        mm({"BLOCK_M": 256, "BLOCK_N": 256, "dtype": "float32", "num_warps": 4})
+    assert "register" in ei.value.log
+
+
+def test_small_tiles_route_to_cuda_cores():
+    res = mm({"BLOCK_M": 32, "BLOCK_N": 32, "BLOCK_K": 16, "num_warps": 4}).resources()
+    assert res["kernel"].startswith("matmul_simt_kernel")
+
+
+def test_attention_plans():
+    base = {"BLOCK_M": 128, "BLOCK_N": 128, "num_warps": 4, "num_stages": 2,
+            "dtype": "bfloat16"}
+    r = compile_module("attention_causal", (128, 4096, 128), base).resources()
+    assert r["kernel"] == "attn_tc_kernel<bf16,BN=128,D=128,causal>"
+    assert r["tmem_cols"] == 512 and r["grid"] == [32, 128, 1]
+    with pytest.raises(KernelBuildError):  # 3 K/V stages of 64 KB do not fit
+        compile_module("attention_causal", (128, 4096, 128), {**base, "num_stages": 3})
+    with pytest.raises(KernelBuildError) as ei:  # fp32 tiles of the CUDA-core family
+        compile_module("attention", (16, 1024, 128), {**base, "dtype": "float32"})
+    assert "shared memory" in ei.value.log
+    with pytest.raises(KernelBuildError) as ei:  # same rule as runner.py:233-234
+        compile_module("attention", (16, 1024, 48), base)
+    assert "power of two" in str(ei.value)
+
+
+def test_unknown_task_and_strategy_are_rejected():
+    with pytest.raises(KernelBuildError):
+        compile_module("conv2d", (8,), {})
+    with pytest.raises(KernelBuildError):
+        compile_module("reduction", (1000,), {"BLOCK_SIZE": 256, "strategy": "tree",
+                                              "dtype": "float32"})
+    with pytest.raises(KernelBuildError):
+        compile_module("reduction", (1000,), {"BLOCK_SIZE": 256, "strategy": "loop",
+                                              "dtype": "bfloat16"})
+
+
+def test_scratch_requirements():
+    r = compile_module("reduction", (100_003,), {"BLOCK_SIZE": 1024, "num_warps": 4,
+                                                 "strategy": "two_pass",
+                                                 "dtype": "float32"}).resources()
+    assert r["scratch_bytes"][0] == 4 * 98 and r["launches_per_call"] == 2
+    r = compile_module("fused_elementwise", (1000,), {"BLOCK_SIZE": 256, "num_warps": 4,
+                                                      "strategy": "unfused",
+                                                      "dtype": "bfloat16"}).resources()
+    assert r["scratch_bytes"] == [2000, 2000] and r["launches_per_call"] == 3
+
+
+def test_render_source_works_without_gpu():
+    """tests/test_triton_gpu.py:73-82, for the CUDA backend."""
+    src = render_source("matmul", {"BLOCK_M": 128, "BLOCK_N": 128, "BLOCK_K": 64,
+                                   "GROUP_M": 4, "num_warps": 4, "num_stages": 3,
+                                   "dtype": "float16"})
+    assert "tcgen05.mma" in src and "matmul_tc_kernel" in src
+    assert "BLOCK_M = 128" in src
+    src_red = render_source("reduction", {"strategy": "atomic", "BLOCK_SIZE": 1024})
+    assert "reduce_slice_kernel" in src_red
+
+
+def test_row_kernel_plans():
+    r = compile_module("softmax", (16384, 8192), {"BLOCK_N": 8192, "num_warps": 8,
+                                                  "num_stages": 1,
+                                                  "dtype": "bfloat16"}).resources()
+    assert r["kernel"] == "softmax_tile_regs<vpt=4>"
+    r = compile_module("softmax", (16384, 8192), {"BLOCK_N": 16384, "num_warps": 4,
+                                                  "num_stages": 1,
+                                                  "dtype": "bfloat16"}).resources()
+    assert r["kernel"] == "softmax_tile_smem<vpt=0>"
+    r = compile_module("layernorm", (37, 500), {"BLOCK_N": 128, "num_warps": 4,
+                                                "num_stages": 1,
+                                                "dtype": "float32"}).resources()
+    assert r["kernel"] == "layernorm_twopass<vpt=1>"

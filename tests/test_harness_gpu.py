@@ -1,0 +1,80 @@
+"""The reference's real-hardware contract (tests/test_triton_gpu.py:32-70),
+run against the B200 backend through the harness."""
+
+import random
+
+import pytest
+
+from gpu_optimizer_b200.harness import BenchmarkSettings, CudaBenchmarkEngine
+from gpu_optimizer_b200.tasks import REFERENCE_TASKS, get_task
+
+pytestmark = pytest.mark.gpu
+
+GPU_SHAPES = {  # tests/test_triton_gpu.py:21-29
+    "matmul": (384, 320, 288), "vecadd": (1_000_003,), "reduction": (1_000_003,),
+    "softmax": (256, 1000), "layernorm": (256, 1000), "fused_elementwise": (1_000_003,),
+    "attention": (4, 512, 64), "attention_causal": (4, 512, 64), "fused_gelu": (1_000_003,),
+}
+ALL = sorted(GPU_SHAPES)
+
+
+@pytest.fixture(scope="module")
+def engine():
+    return CudaBenchmarkEngine(settings=BenchmarkSettings(warmup=3, iterations=10))
+
+
+@pytest.mark.parametrize("name", ALL)
+def test_kernel_correct_on_gpu_default_config(engine, name):
+    task = get_task(name)
+    shape = GPU_SHAPES[name]
+    res = engine.benchmark_candidate(task, task.make_candidate(shape, task.default_config(shape)))
+    assert res.status == "ok", f"{name}: {res.error}"
+    assert res.correct and res.correctness_mode == "device"
+    assert res.latency.median_ms > 0 and res.engine == "cuda"
+
+
+@pytest.mark.parametrize("name", ALL)
+def test_kernel_correct_on_gpu_random_configs(engine, name):
+    task = get_task(name)
+    shape = GPU_SHAPES[name]
+    space = task.param_space(shape)
+    rng = random.Random(0)
+    ok = 0
+    for _ in range(6):
+        cand = task.make_candidate(shape, space.sample(rng), provenance="random")
+        res = engine.benchmark_candidate(task, cand)
+        # compile errors are legitimate (resource limits); wrong answers are not
+        assert res.status in ("ok", "compile_error"), f"{name} {cand.config}: {res.error}"
+        ok += res.status == "ok"
+    assert ok >= 1
+
+
+B200_SMALL = {"matmul": (1024, 1024, 1024), "vecadd": (1 << 20,), "reduction": (1 << 20,),
+              "softmax": (512, 8192), "layernorm": (512, 8192), "fused_elementwise": (1 << 20,),
+              "fused_gelu": (1 << 20,), "attention": (8, 1024, 128),
+              "attention_causal": (8, 1024, 128)}
+
+
+@pytest.mark.parametrize("name", ALL)
+def test_b200_space_random_configs(engine, name):
+    task = get_task(name, "b200")
+    shape = B200_SMALL[name]
+    space = task.param_space(shape)
+    rng = random.Random(1)
+    statuses = []
+    for _ in range(8):
+        cand = task.make_candidate(shape, space.sample(rng), provenance="random")
+        res = engine.benchmark_candidate(task, cand)
+        assert res.status in ("ok", "compile_error"), f"{name} {cand.config}: {res.error}"
+        statuses.append(res.status)
+    assert "ok" in statuses
+
+
+def test_baseline_and_roofline_fields(engine):
+    task = get_task("vecadd", "b200")
+    shape = (1 << 24,)
+    base = engine.benchmark_baseline(task, shape, "float32")
+    assert base.ok and base.achieved_unit == "GB/s" and base.achieved > 0
+    res = engine.benchmark_candidate(task, task.make_candidate(
+        shape, {"BLOCK_SIZE": 4096, "num_warps": 8, "dtype": "float32"}))
+    assert res.ok and 0 < res.roofline_fraction < 1.5
