@@ -1,0 +1,108 @@
+"""Sharded candidate evaluation: worker pool, failure handling, gloo ranks.
+
+All failures are made on the host (an exception, a worker process that
+exits, a worker that sleeps past its deadline); no GPU is used.
+"""
+
+import os
+import socket
+
+import pytest
+import torch.distributed as dist
+import torch.multiprocessing as tmp
+
+import fake_engine
+from gpu_optimizer_b200 import distributed as D
+from gpu_optimizer_b200.dispatch import MultiDeviceEvaluator
+from gpu_optimizer_b200.search import (GridSearcher, RandomSearcher, SearchLoop,
+                                       compute_reward)
+from gpu_optimizer_b200.space import Candidate, ParamSpace, ParamSpec
+from gpu_optimizer_b200.harness import BenchmarkResult, LatencyStats
+
+
+def cands(modes):
+    return [Candidate("vecadd", (1024,), {"BLOCK_SIZE": 2 ** (i % 8 + 1), "mode": m,
+                                          "i": i}) for i, m in enumerate(modes)]
+
+
+def test_results_come_back_in_proposal_order():
+    with MultiDeviceEvaluator([0, 1, 2], factory=fake_engine.factory,
+                              pin_devices=False) as ev:
+        cs = cands(["ok"] * 17)
+        res = ev.evaluate(cs)
+    assert [r.candidate_id for r in res] == [c.candidate_id for c in cs]
+    assert all(r.status == "ok" for r in res)
+    assert len({r.worker_id for r in res}) > 1  # work was spread
+
+
+def test_worker_exception_crash_and_hang_are_contained():
+    with MultiDeviceEvaluator([0, 1], factory=fake_engine.factory, pin_devices=False,
+                              candidate_timeout_s=3.0) as ev:
+        cs = cands(["ok", "raise", "ok", "crash", "ok", "hang", "ok", "ok"])
+        res = ev.evaluate(cs)
+        statuses = [r.status for r in res]
+        assert statuses == ["ok", "runtime_error", "ok", "runtime_error", "ok",
+                            "runtime_error", "ok", "ok"]
+        assert "synthetic failure" in res[1].error
+        assert "died" in res[3].error and "timeout" in res[5].error
+        assert ev.respawns >= 2
+        # the pool still serves after the failures
+        again = ev.evaluate(cands(["ok"] * 4))
+        assert all(r.status == "ok" for r in again)
+
+
+def test_search_loop_dedupes_and_tracks_best():
+    space = ParamSpace([ParamSpec("BLOCK_SIZE", (2, 4, 8, 16)), ParamSpec("mode", ("ok",))])
+    with MultiDeviceEvaluator([0, 1], factory=fake_engine.factory, pin_devices=False) as ev:
+        out = SearchLoop("vecadd", (1024,), GridSearcher("vecadd", (1024,), space), ev,
+                         baseline_ms=1.0, max_evaluations=10, batch_size=3).run()
+    assert out.candidates_evaluated == 4  # grid exhausted, no duplicates
+    assert out.best_candidate.config["BLOCK_SIZE"] == 16
+    rs = RandomSearcher("vecadd", (1024,), space, seed=0).propose(3)
+    assert len(rs) == 3
+
+
+def test_reward_matches_reference_rules():
+    base = dict(candidate_id="x", task="t", shape=(1,), config={}, engine="cuda",
+                gpu_name="g")
+    ok = BenchmarkResult(**base, status="ok", latency=LatencyStats.from_samples([0.5, 0.5]))
+    assert compute_reward(ok, 1.0) == pytest.approx(1.0)
+    assert compute_reward(BenchmarkResult(**base, status="compile_error"), 1.0) == -0.5
+    assert compute_reward(BenchmarkResult(**base, status="runtime_error"), 1.0) == -0.8
+    assert compute_reward(BenchmarkResult(**base, status="incorrect"), 1.0) == -1.0
+
+
+def test_shard_unshard_roundtrip():
+    items = list(range(23))
+    parts = [D.shard(items, r, 4) for r in range(4)]
+    assert sorted(sum(parts, [])) == items
+    assert D.unshard(parts, len(items)) == items
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _rank_main(rank, world, port):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        items = list(range(10))
+        mine = D.shard(items, rank, world)
+        # each rank "evaluates" its shard; time differs per rank
+        t = 1.0 + rank
+        assert D.reduce_scalar(t, "max") == world
+        assert D.reduce_scalar(len(mine), "sum") == len(items)
+        parts = D.gather_objects([x * 10 for x in mine])
+        assert D.unshard(parts, len(items)) == [x * 10 for x in items]
+        D.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+def test_gloo_world_size_two_sharding():
+    tmp.spawn(_rank_main, args=(2, _free_port()), nprocs=2, join=True)
