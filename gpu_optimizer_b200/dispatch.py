@@ -136,6 +136,25 @@ class MultiDeviceEvaluator:
         self.respawns += 1
         self._workers[w.wid] = self._spawn(w.wid, w.device)
 
+    def wait_ready(self, timeout_s: float = 600.0) -> bool:
+        """Block until every worker has built its engine (or the deadline)."""
+        t0 = time.time()
+        while time.time() - t0 < timeout_s:
+            pending = [w for w in self._workers if not w.ready]
+            if not pending:
+                return True
+            for c in mpc.wait([w.conn for w in pending], timeout=0.2):
+                w = next(x for x in pending if x.conn is c)
+                try:
+                    if w.conn.recv() == "ready":
+                        w.ready = True
+                except (EOFError, OSError):
+                    self._replace(w)
+            for w in pending:
+                if not w.ready and not w.proc.is_alive():
+                    self._replace(w)
+        return all(w.ready for w in self._workers)
+
     def evaluate(self, candidates: Sequence[Candidate]) -> list[BenchmarkResult]:
         """Results in the order of ``candidates``.
 

@@ -28,6 +28,7 @@ def cands(modes):
 def test_results_come_back_in_proposal_order():
     with MultiDeviceEvaluator([0, 1, 2], factory=fake_engine.factory,
                               pin_devices=False) as ev:
+        assert ev.wait_ready(120)
         cs = cands(["ok"] * 17)
         res = ev.evaluate(cs)
     assert [r.candidate_id for r in res] == [c.candidate_id for c in cs]
