@@ -52,7 +52,7 @@ def parse_args():
     ap.add_argument("--steps", type=int, default=10000)
     ap.add_argument("--warmup", type=int, default=50)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
-    ap.add_argument("--no-extras", action="store_true", help="skip per-task and search lines")
+    ap.add_argument("--no-extras", action="store_true", help="skip the per-task, search and CPU-baseline legs")
     return ap.parse_args()
 
 
@@ -407,7 +407,7 @@ def main():
             line["search"] = {"error": str(e)[:200]}
         if world == 1:
             line["tasks"] = run_extras(world)
-    if rank == 0 and world == 1:
+    if rank == 0 and world == 1 and not args.no_extras:
         line["cpu_baseline"] = cpu_baseline()
     if rank == 0:
         print(json.dumps(line), flush=True)
