@@ -76,6 +76,9 @@ SIGNATURES = {
     "gpo_device_status": (ctypes.c_int, [ctypes.c_void_p, ctypes.POINTER(ctypes.c_uint32)]),
     "gpo_selftest_timeout": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_uint32,
                                             ctypes.POINTER(ctypes.c_uint32)]),
+    "gpo_reduction_sum_noalloc": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int64,
+                                                 ctypes.c_void_p, ctypes.c_int32,
+                                                 ctypes.c_int32, ctypes.c_void_p]),
     "gpo_destroy": (None, [ctypes.c_void_p]),
     "gpo_source": (ctypes.c_char_p, [ctypes.c_void_p]),
     "gpo_status_name": (ctypes.c_char_p, [ctypes.c_int]),
@@ -186,3 +189,14 @@ def selftest_timeout(stream: int, limit_ms: int = 100) -> tuple[int, int]:
     flags = ctypes.c_uint32(0)
     rc = load().gpo_selftest_timeout(ctypes.c_void_p(stream), limit_ms, ctypes.byref(flags))
     return rc, int(flags.value)
+
+
+NOALLOC_MAX_PARTIALS = 65536
+
+
+def reduction_sum_noalloc(x_ptr: int, n: int, out_ptr: int, block_size: int, num_warps: int,
+                          stream: int) -> int:
+    """gpo_reduction_sum_noalloc: two_pass fp32 sum with the library's fixed
+    partial-sum array (no allocation); returns the gpo_status code."""
+    return load().gpo_reduction_sum_noalloc(ctypes.c_void_p(x_ptr), n, ctypes.c_void_p(out_ptr),
+                                            block_size, num_warps, ctypes.c_void_p(stream))

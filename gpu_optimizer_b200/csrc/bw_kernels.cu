@@ -9,6 +9,7 @@
 // slice start and the three base pointers are 16-byte aligned; a scalar path
 // covers the ragged tail and unaligned views.
 #include <algorithm>
+#include <mutex>
 
 #include "gpo_common.cuh"
 #include "gpo_internal.h"
@@ -409,4 +410,76 @@ gpo_status launch_selftest_timeout(const LaunchCtx& c, unsigned long long limit_
   return launch_status();
 }
 
+// ------------------------------------------------- allocation-free two_pass
+// Some callers cannot allocate device memory at the point where they need a
+// sum: code running inside a CUDA stream capture that must not add
+// allocations to the graph, host runtimes with their own fixed device-memory
+// budget, or plug-in hosts that hand this library only input and output
+// buffers.  For them gpo_reduction_sum_noalloc runs the two_pass reduction
+// with its partial sums in the fixed array below instead of a caller buffer.
+//
+// The array is part of the library image: every GPU that loads the library
+// holds it (256 KiB) until the process exits.  All calls on a device share
+// it, so calls whose kernels overlap on the GPU (different streams, no
+// ordering between them) race on it; calls on one stream are ordered.
+// Each call writes every partial it later reads, so nothing needs clearing;
+// the array keeps whatever the last call left.
+constexpr int64_t kNoAllocMaxPartials = 65536;
+static __device__ __align__(256) float g_noalloc_partials[kNoAllocMaxPartials];
+
+namespace {
+constexpr int kNoAllocDevices = 64;
+std::mutex g_noalloc_mu;
+float* g_noalloc_ptr[kNoAllocDevices] = {nullptr};
+}  // namespace
+
+// Device address of g_noalloc_partials on the current device.  In host code
+// the array's name is only a host-side stand-in, so the address is resolved
+// once per device with that device current.
+static gpo_status noalloc_scratch(float** out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) {
+    cudaGetLastError();
+    return GPO_NO_DEVICE;
+  }
+  if (dev < 0 || dev >= kNoAllocDevices) return GPO_NO_DEVICE;
+  std::lock_guard<std::mutex> lk(g_noalloc_mu);
+  if (!g_noalloc_ptr[dev]) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_partials);
+    if (e != cudaSuccess || !p) {
+      cudaGetLastError();
+      return GPO_LAUNCH_ERROR;
+    }
+    g_noalloc_ptr[dev] = static_cast<float*>(p);
+  }
+  *out = g_noalloc_ptr[dev];
+  return GPO_OK;
+}
+
 }  // namespace gpo
+
+extern "C" gpo_status gpo_reduction_sum_noalloc(const float* x, int64_t n, float* out,
+                                                int32_t block_size, int32_t num_warps,
+                                                void* stream) {
+  using namespace gpo;
+  if (!x || !out || n < 0 || block_size < 1 || block_size > (1 << 20) || num_warps < 1 ||
+      num_warps > 32)
+    return GPO_BAD_ARGS;
+  const int64_t nblocks = n == 0 ? 0 : static_cast<int64_t>(cdiv(n, block_size));
+  if (nblocks > kNoAllocMaxPartials) return GPO_BAD_ARGS;  // n > 65536 * block_size
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (n == 0) {
+    return cudaMemsetAsync(out, 0, sizeof(float), st) == cudaSuccess ? GPO_OK
+                                                                       : GPO_LAUNCH_ERROR;
+  }
+  float* partial = nullptr;
+  gpo_status s = noalloc_scratch(&partial);
+  if (s != GPO_OK) return s;
+  const int vec = (aligned16(x) && block_size % 4 == 0) ? 1 : 0;
+  reduce_slice_kernel<false><<<static_cast<unsigned>(nblocks), num_warps * 32, 0, st>>>(
+      x, partial, n, block_size, vec);
+  s = launch_status();
+  if (s != GPO_OK) return s;
+  return run_loop(partial, out, nblocks, block_size, num_warps, st);
+}

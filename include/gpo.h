@@ -168,6 +168,27 @@ GPO_API gpo_status gpo_device_status(void* stream, uint32_t* flags);
  * (benchmarks/harness.py:144-203). */
 GPO_API gpo_status gpo_selftest_timeout(void* stream, uint32_t limit_ms, uint32_t* flags);
 
+/* Sum of n fp32 values with the two_pass algorithm (per-slice partial sums,
+ * then one CTA summing the partials), without allocating anything: the
+ * partial sums live in a fixed 65536-float array inside the library, so a
+ * caller that cannot allocate device memory (inside a stream capture, under
+ * a host runtime's fixed memory budget, or as a plug-in given only its input
+ * and output buffers) passes just x (device, n floats), out (device, one
+ * float), BLOCK_SIZE and num_warps.  Same kernels and numerics as the
+ * two_pass strategy of gpo_launch.
+ *  - Limit: cdiv(n, block_size) <= 65536, i.e. n <= 65536 * block_size;
+ *    larger n returns GPO_BAD_ARGS before anything is launched.
+ *  - The first call on a device looks up the array's device address; make
+ *    that first call before any stream capture.
+ *  - All calls on a device share the array: calls whose kernels may overlap
+ *    on the GPU (unordered streams) race; calls on one stream do not.
+ *  - No cudaMalloc, cudaFree or other allocation is made by this call.
+ * No counterpart in the reference, whose runner allocates the partials with
+ * torch at build time. */
+GPO_API gpo_status gpo_reduction_sum_noalloc(const float* x, int64_t n, float* out,
+                                             int32_t block_size, int32_t num_warps,
+                                             void* stream);
+
 /* Free a module. */
 GPO_API void gpo_destroy(gpo_module* mod);
 
