@@ -204,9 +204,7 @@ gpo_status plan_matmul(const gpo_key& k, Plan& p, std::string& log) {
     return GPO_BAD_CONFIG;
   }
   const int es = dtype_bytes(k.dtype);
-  // tf32 stays on CUDA cores (inputs truncated to tf32) until the tcgen05
-  // kind::tf32 path with an MN-major B operand is validated on hardware.
-  const bool tc_dtype = k.dtype == GPO_BFLOAT16 || k.dtype == GPO_FLOAT16;
+  const bool tc_dtype = k.dtype != GPO_FLOAT32;
   const bool tc_tile = (k.block_m == 128 || k.block_m == 256) && k.block_n >= 32 &&
                        k.block_k * es >= 32 && (k.num_warps == 4 || k.num_warps == 8);
   const bool tc_shape = (k.shape[2] * es) % 16 == 0 && (k.shape[1] * es) % 16 == 0;

@@ -181,8 +181,13 @@ __global__ void __launch_bounds__(PERSISTENT ? 256 : 128, 1)
         for (int kk = 0; kk < ksteps; ++kk) {
           const uint32_t kbyte = static_cast<uint32_t>(kk) * 32u;
           const uint32_t a_off = (kbyte / swa) * (BM * swa) + (kbyte % swa);
+          // MN-major B.  16-bit: 128/64/32-byte swizzle atoms of 8 K rows.
+          // tf32: 32-bit MN-major operands use the 128-byte swizzle with
+          // 32-byte atoms (layout type 1) and 4-row K groups.
           const uint64_t bdesc =
-              make_smem_desc(sb + kk * KSTEP * SWB, BK * SWB, 8 * SWB, SWB);
+              FMT == 2 ? (make_smem_desc(sb + kk * KSTEP * SWB, BK * SWB, 4 * SWB, 0) |
+                          (1ull << 61))
+                       : make_smem_desc(sb + kk * KSTEP * SWB, BK * SWB, 8 * SWB, SWB);
 #pragma unroll
           for (int h = 0; h < HALVES; ++h) {
             const uint64_t adesc = make_smem_desc(sa + a_off + h * 128 * swa, 16, 8 * swa, swa);
@@ -275,7 +280,10 @@ typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t,
                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
 
-static CUtensorMapSwizzle swizzle_enum(int bytes) {
+// bytes = 128 / 64 / 32; atom32 selects the 128-byte swizzle with 32-byte
+// atoms that 32-bit MN-major tensor-core operands need.
+static CUtensorMapSwizzle swizzle_enum(int bytes, bool atom32 = false) {
+  if (atom32) return CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B;
   return bytes == 128 ? CU_TENSOR_MAP_SWIZZLE_128B
          : bytes == 64 ? CU_TENSOR_MAP_SWIZZLE_64B
                        : CU_TENSOR_MAP_SWIZZLE_32B;
@@ -284,7 +292,8 @@ static CUtensorMapSwizzle swizzle_enum(int bytes) {
 // 2-D row-major tensor [rows, cols] (cols contiguous) with box
 // [box_rows, box_cols].
 static bool encode_2d(CUtensorMap* map, CUtensorMapDataType dt, const void* ptr, uint64_t rows,
-                      uint64_t cols, int es, uint32_t box_cols, uint32_t box_rows, int swz) {
+                      uint64_t cols, int es, uint32_t box_cols, uint32_t box_rows, int swz,
+                      bool atom32 = false) {
   EncodeTiledFn fn = reinterpret_cast<EncodeTiledFn>(tensor_map_encoder());
   if (!fn) return false;
   const cuuint64_t dims[2] = {cols, rows};
@@ -292,7 +301,7 @@ static bool encode_2d(CUtensorMap* map, CUtensorMapDataType dt, const void* ptr,
   const cuuint32_t box[2] = {box_cols, box_rows};
   const cuuint32_t estr[2] = {1, 1};
   CUresult r = fn(map, dt, 2, const_cast<void*>(ptr), dims, strides, box, estr,
-                  CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle_enum(swz),
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle_enum(swz, atom32),
                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS;
 }
@@ -377,7 +386,8 @@ static gpo_status run_tc(const gpo_key& k, const Plan& p, const gpo_args& a, con
   constexpr int SWB = (BN * sizeof(T)) < 128 ? (BN * sizeof(T)) : 128;
   CUtensorMap ma, mb;
   if (!encode_2d(&ma, dt, a.in[0], M, K, es, swa / es, BM, swa)) return GPO_LAUNCH_ERROR;
-  if (!encode_2d(&mb, dt, a.in[1], K, N, es, SWB / es, k.block_k, SWB)) return GPO_LAUNCH_ERROR;
+  if (!encode_2d(&mb, dt, a.in[1], K, N, es, SWB / es, k.block_k, SWB, FMT == 2))
+    return GPO_LAUNCH_ERROR;
   auto kern = matmul_tc_kernel<T, FMT, BM, BN, P>;
   const uint32_t dyn = static_cast<uint32_t>(p.aux[1]);
   gpo_status s = ensure_smem_attr(reinterpret_cast<const void*>(kern), dyn);

@@ -138,10 +138,13 @@ def default_peaks() -> dict:
         try:
             d = json.loads(p.read_text())
             return {"hbm_gbs": float(d["hbm_gbs"]), "bf16_tflops": float(d["bf16_tflops"]),
+                    "bf16_tflops_sustained": float(d.get("bf16_tflops_sustained",
+                                                         d["bf16_tflops"])),
                     "source": "measured"}
         except Exception:
             pass
-    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "source": "fallback"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0,
+            "source": "fallback"}
 
 
 class CudaBenchmarkEngine:
