@@ -2,6 +2,7 @@
 // launch dispatch, per-device error word, embedded kernel sources.
 // Declarations and the reference interface each entry point replaces are in
 // include/gpo.h.
+#include <algorithm>
 #include <cstring>
 #include <map>
 #include <mutex>
@@ -120,6 +121,30 @@ gpo_status ensure_smem_attr(const void* func, uint32_t dyn_smem) {
   uint32_t& v = g_smem_attr[{func, dev}];
   if (v < dyn_smem) v = dyn_smem;
   return GPO_OK;
+}
+
+unsigned persistent_grid(const void* func, int threads, size_t dyn_smem, int sm_count,
+                         int64_t work_items) {
+  static std::mutex mu;
+  static std::map<std::pair<const void*, int>, int> occ;
+  int per_sm = 0;
+  {
+    std::lock_guard<std::mutex> lk(mu);
+    auto it = occ.find({func, threads});
+    if (it != occ.end()) per_sm = it->second;
+  }
+  if (per_sm == 0) {
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, func, threads, dyn_smem) !=
+            cudaSuccess ||
+        per_sm < 1) {
+      cudaGetLastError();
+      per_sm = 1;
+    }
+    std::lock_guard<std::mutex> lk(mu);
+    occ[{func, threads}] = per_sm;
+  }
+  const int64_t g = static_cast<int64_t>(per_sm) * (sm_count > 0 ? sm_count : 148);
+  return static_cast<unsigned>(std::max<int64_t>(1, std::min<int64_t>(g, work_items)));
 }
 
 void* tensor_map_encoder() {

@@ -246,29 +246,42 @@ __global__ void __launch_bounds__(256, 1)
         break;
       }
       tc_fence_after();
+      // all BN/32 TMEM loads in flight before a single wait
       float sv[BN];
+      {
+        uint32_t r[BN];
 #pragma unroll
-      for (int c = 0; c < BN / 32; ++c) {
-        uint32_t r[32];
-        tmem_ld32(tmem + lane_addr + static_cast<uint32_t>(D + b * BN + c * 32), r);
+        for (int c = 0; c < BN / 32; ++c)
+          tmem_ld32(tmem + lane_addr + static_cast<uint32_t>(D + b * BN + c * 32),
+                    *reinterpret_cast<uint32_t(*)[32]>(r + c * 32));
         tmem_wait_ld();
 #pragma unroll
-        for (int i = 0; i < 32; ++i) sv[c * 32 + i] = __uint_as_float(r[i]);
+        for (int i = 0; i < BN; ++i) sv[i] = __uint_as_float(r[i]);
       }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(smem_u32(&sh.s_free[b]));
 
-      // scale into the log2 domain and mask padding / future keys
+      // Mask padding / future keys only where the block needs it (block-
+      // uniform test on the tile's first row); work on raw scores, with the
+      // log2-domain scale folded into the exponent's FMA below.
       const int key0 = j * BN;
-      float mb = -INFINITY;
+      const bool need_mask = key0 + BN > S || (CAUSAL && key0 + BN - 1 > q0);
+      if (need_mask) {
 #pragma unroll
-      for (int i = 0; i < BN; ++i) {
-        const int key = key0 + i;
-        const bool masked = key >= S || (CAUSAL && key > qrow);
-        sv[i] = masked ? -INFINITY : sv[i] * scale_log2;
-        mb = fmaxf(mb, sv[i]);
+        for (int i = 0; i < BN; ++i) {
+          const int key = key0 + i;
+          if (key >= S || (CAUSAL && key > qrow)) sv[i] = -INFINITY;
+        }
       }
+      float mx8[8];
+#pragma unroll
+      for (int t = 0; t < 8; ++t) mx8[t] = sv[t];
+#pragma unroll
+      for (int i = 8; i < BN; ++i) mx8[i & 7] = fmaxf(mx8[i & 7], sv[i]);
+      const float mb = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
+                             fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7]))) *
+                       scale_log2;
       if (j == 0) {
         m_used = mb;
       } else {
@@ -299,14 +312,15 @@ __global__ void __launch_bounds__(256, 1)
           m_used = m_new;
         }
       }
-      // P_j = exp2(s - m_used); the P buffer b is free once PV_{j-2} is done
-      float rs = 0.f;
+      // P_j = exp2(s * scale - m_used); 8 independent partial sums
+      const float neg_m = (m_used == -INFINITY) ? 0.f : -m_used;
+      float rs8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
 #pragma unroll
       for (int i = 0; i < BN; ++i) {
-        sv[i] = (m_used == -INFINITY) ? 0.f : ex2_approx(sv[i] - m_used);
-        rs += sv[i];
+        sv[i] = ex2_approx(fmaf(sv[i], scale_log2, neg_m));  // -inf -> 0
+        rs8[i & 7] += sv[i];
       }
-      l += rs;
+      l += ((rs8[0] + rs8[1]) + (rs8[2] + rs8[3])) + ((rs8[4] + rs8[5]) + (rs8[6] + rs8[7]));
       if (j >= 2) {
         const int pj = j - 2;
         if (!mbar_wait(smem_u32(&sh.pv_done[pj & 1]), static_cast<uint32_t>(pj >> 1) & 1u,

@@ -68,21 +68,37 @@ __global__ void __launch_bounds__(1024) ew_kernel(const T* __restrict__ a, const
     const uint4* av = reinterpret_cast<const uint4*>(a + base);
     const uint4* bv = reinterpret_cast<const uint4*>(ew_binary<OP>() ? b + base : a + base);
     uint4* ov = reinterpret_cast<uint4*>(out + base);
-#pragma unroll 4
-    for (int64_t i = threadIdx.x; i < nvec; i += blockDim.x) {
-      uint4 ra = __ldcs(av + i);
-      uint4 rb;
-      if constexpr (ew_binary<OP>()) rb = __ldcs(bv + i);
-      const T* ea = reinterpret_cast<const T*>(&ra);
-      const T* eb = reinterpret_cast<const T*>(&rb);
-      uint4 ro;
-      T* eo = reinterpret_cast<T*>(&ro);
+    // Batches of EW_BATCH vectors per thread: every load of a batch is
+    // issued before the first store, so each thread keeps up to
+    // 2 * EW_BATCH 16-byte loads in flight.
+    constexpr int EW_BATCH = 4;
+    const int64_t T_ = blockDim.x;
+    for (int64_t i0 = threadIdx.x; i0 < nvec; i0 += EW_BATCH * T_) {
+      uint4 ra[EW_BATCH], rb[EW_BATCH];
 #pragma unroll
-      for (int j = 0; j < V; ++j) {
-        const float fb = ew_binary<OP>() ? E::to_f(eb[j]) : 0.f;
-        eo[j] = E::from_f(ew_apply<OP>(E::to_f(ea[j]), fb, s));
+      for (int u = 0; u < EW_BATCH; ++u) {
+        const int64_t i = i0 + u * T_;
+        if (i < nvec) {
+          ra[u] = __ldcs(av + i);
+          if constexpr (ew_binary<OP>()) rb[u] = __ldcs(bv + i);
+        }
       }
-      __stcs(ov + i, ro);
+#pragma unroll
+      for (int u = 0; u < EW_BATCH; ++u) {
+        const int64_t i = i0 + u * T_;
+        if (i < nvec) {
+          const T* ea = reinterpret_cast<const T*>(&ra[u]);
+          const T* eb = reinterpret_cast<const T*>(&rb[u]);
+          uint4 ro;
+          T* eo = reinterpret_cast<T*>(&ro);
+#pragma unroll
+          for (int j = 0; j < V; ++j) {
+            const float fb = ew_binary<OP>() ? E::to_f(eb[j]) : 0.f;
+            eo[j] = E::from_f(ew_apply<OP>(E::to_f(ea[j]), fb, s));
+          }
+          __stcs(ov + i, ro);
+        }
+      }
     }
     done = nvec * V;
   }

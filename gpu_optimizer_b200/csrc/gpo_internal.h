@@ -82,6 +82,11 @@ inline gpo_status launch_status() {
 // Set the dynamic shared memory opt-in of a kernel once per device.
 gpo_status ensure_smem_attr(const void* func, uint32_t dyn_smem);
 
+// Grid of a persistent kernel: SM count x resident CTAs per SM (occupancy
+// of `func` at `threads` / `dyn_smem`, cached), at most `work_items`.
+unsigned persistent_grid(const void* func, int threads, size_t dyn_smem, int sm_count,
+                         int64_t work_items);
+
 // Driver entry point for cuTensorMapEncodeTiled, resolved once.
 void* tensor_map_encoder();
 

@@ -7,8 +7,10 @@
 // (runner.py:101), fp32 accumulation in TMEM.
 //
 // Config mapping (one instantiation per (dtype, BLOCK_M, BLOCK_N, warps)):
-//   BLOCK_M    : 128 -> one M=128 MMA per K step; 256 -> two M=128 MMAs into
-//                two TMEM accumulators sharing the B tile.
+//   BLOCK_M    : 128 -> one M=128 MMA per K step.  256 with 4 warps -> a CTA
+//                pair (cluster of 2, cta_group::2 M=256 MMAs, each CTA
+//                staging half of B; matmul_tc2_kernel).  256 with 8 warps ->
+//                two M=128 MMAs per CTA into two TMEM accumulators sharing B.
 //   BLOCK_N    : MMA N and TMEM columns per accumulator.
 //   BLOCK_K    : K extent of one TMA stage (runtime); the MMA issuer walks it
 //                in 32-byte K steps (16 bf16/fp16 or 8 tf32 elements).
@@ -274,6 +276,202 @@ __global__ void __launch_bounds__(PERSISTENT ? 256 : 128, 1)
   if (warp == alloc_warp) tmem_dealloc(tmem_base, ALLOC);
 }
 
+// --------------------------------------------------- CTA-pair (2-SM) tile
+// BLOCK_M = 256 with num_warps = 4: a cluster of two CTAs computes one
+// 256 x BLOCK_N tile with M=256 tcgen05 MMAs issued by the even CTA
+// (cta_group::2).  CTA r holds A rows [128r, 128r+128) and B columns
+// [r*BN/2, (r+1)*BN/2) of the tile, so each CTA stages only half of B:
+// 32 KB per 64-deep K stage for a 256x256 tile instead of 48 KB for a
+// single-CTA 128x256 tile, which lets more stages (more load latency cover)
+// fit per SM.  Each CTA's TMEM receives its own 128 rows of D.
+//
+// Barriers: full[s] lives in the even CTA only; its producer arms it with
+// the bytes of both CTAs and both producers' TMA loads count their bytes on
+// it.  empty[s] and acc_full live in both CTAs; the even CTA's MMA thread
+// commits to its own and (through the cluster address) to the peer's.
+// All waits are bounded; a CTA that gives up drains and still reaches the
+// final cluster barrier, so neither CTA exits while the other can signal it.
+template <typename T, int FMT, int BN>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(128, 1)
+    matmul_tc2_kernel(const __grid_constant__ CUtensorMap tma_a,
+                      const __grid_constant__ CUtensorMap tma_b, T* __restrict__ C, int M, int N,
+                      int K, int BK, int stages, int group_m, int swa, unsigned int* err) {
+  constexpr int ES = sizeof(T);
+  constexpr int BNH = BN / 2;                                 // B columns per CTA
+  constexpr int SWB = (BNH * ES) < 128 ? (BNH * ES) : 128;    // B chunk width (bytes)
+  constexpr int ALLOC = BN <= 32 ? 32 : BN <= 64 ? 64 : BN <= 128 ? 128 : 256;
+  constexpr int KSTEP = 32 / ES;
+  constexpr uint32_t IDESC = make_idesc(FMT, 256, BN, false, true);
+
+  __shared__ TcShared sh;
+  extern __shared__ uint8_t dyn_smem[];
+  const uint32_t smem_base = (smem_u32(dyn_smem) + 1023u) & ~1023u;
+  const uint32_t a_bytes = 128u * BK * ES;
+  const uint32_t b_bytes = static_cast<uint32_t>(BK) * BNH * ES;
+  const uint32_t stage_bytes = (a_bytes + b_bytes + 1023u) & ~1023u;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const int num_pid_m = (M + 255) / 256;
+  const int num_pid_n = (N + BN - 1) / BN;
+  const int tile = static_cast<int>(blockIdx.x >> 1);
+  const int num_kb = (K + BK - 1) / BK;
+  int pm, pn;
+  tile_coords(tile, num_pid_m, num_pid_n, group_m, pm, pn);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < stages; ++s) {
+      mbar_init(smem_u32(&sh.full[s]), 1);
+      mbar_init(smem_u32(&sh.empty[s]), 1);
+    }
+    mbar_init(smem_u32(&sh.acc_full[0]), 1);
+    mbar_init(smem_u32(&sh.drain), 1);
+    sh.abort = 0;
+    fence_barrier_init();
+    tma_prefetch_desc(&tma_a);
+    tma_prefetch_desc(&tma_b);
+  }
+  if (warp == 0) {
+    tmem_alloc_pair(smem_u32(&sh.tmem_base), ALLOC);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  cluster_sync_all();  // both CTAs' barriers initialised before any remote signal
+  tc_fence_after();
+  const uint32_t tmem_base = sh.tmem_base;
+  volatile int* abort_flag = &sh.abort;
+
+  if (warp == 0 && lane == 0) {
+    // ------------------------------------------------------ producers (both)
+    const uint32_t full0 = mapa_shared(smem_u32(&sh.full[0]), 0);  // even CTA's full[0]
+    int it = 0;
+    bool ok = true;
+    for (int kb = 0; kb < num_kb; ++kb, ++it) {
+      const int s = it % stages;
+      const uint32_t r = static_cast<uint32_t>(it / stages);
+      if (!mbar_wait(smem_u32(&sh.empty[s]), (r & 1u) ^ 1u, abort_flag, err,
+                     kErrWaitProducer)) {
+        ok = false;
+        break;
+      }
+      const uint32_t full = full0 + static_cast<uint32_t>(s) * 8u;
+      if (rank == 0) mbar_arrive_expect_tx(smem_u32(&sh.full[s]), 2u * (a_bytes + b_bytes));
+      const uint32_t sa = smem_base + s * stage_bytes;
+      const uint32_t sb = sa + a_bytes;
+      const int a_atoms = (BK * ES) / swa;
+      for (int a = 0; a < a_atoms; ++a)
+        tma_load_2d_pair(sa + a * 128 * swa, &tma_a, full, kb * BK + a * (swa / ES),
+                         pm * 256 + static_cast<int>(rank) * 128);
+#pragma unroll
+      for (int c = 0; c < (BNH * ES) / SWB; ++c)
+        tma_load_2d_pair(sb + c * BK * SWB, &tma_b, full,
+                         pn * BN + static_cast<int>(rank) * BNH + c * (SWB / ES), kb * BK);
+    }
+    if (!ok) {
+      if (rank == 0) {
+        for (int j = max(0, it - stages); j < it; ++j)
+          mbar_wait_drain(smem_u32(&sh.full[j % stages]), static_cast<uint32_t>(j / stages) & 1u,
+                          err);
+      } else {
+        // the odd CTA's loads complete on the even CTA's barrier, which it
+        // cannot poll: give in-flight copies time to land before exiting
+        const unsigned long long t0 = globaltimer_ns();
+        while (globaltimer_ns() - t0 < 200000ull) __nanosleep(1000);
+      }
+    }
+  } else if (warp == 1 && lane == 0 && rank == 0) {
+    // --------------------------------------------- MMA issuer (even CTA)
+    const uint32_t peer_empty0 = mapa_shared(smem_u32(&sh.empty[0]), 1);
+    const uint32_t peer_acc = mapa_shared(smem_u32(&sh.acc_full[0]), 1);
+    int it = 0;
+    bool ok = true;
+    for (int kb = 0; kb < num_kb; ++kb, ++it) {
+      const int s = it % stages;
+      const uint32_t r = static_cast<uint32_t>(it / stages);
+      if (!mbar_wait(smem_u32(&sh.full[s]), r & 1u, abort_flag, err, kErrWaitMma)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const uint32_t sa = smem_base + s * stage_bytes;
+      const uint32_t sb = sa + a_bytes;
+      for (int kk = 0; kk < BK / KSTEP; ++kk) {
+        const uint32_t kbyte = static_cast<uint32_t>(kk) * 32u;
+        const uint64_t adesc =
+            make_smem_desc(sa + (kbyte / swa) * (128 * swa) + (kbyte % swa), 16, 8 * swa, swa);
+        const uint64_t bdesc =
+            FMT == 2 ? (make_smem_desc(sb + kk * KSTEP * SWB, BK * SWB, 4 * SWB, 0) |
+                        (1ull << 61))
+                     : make_smem_desc(sb + kk * KSTEP * SWB, BK * SWB, 8 * SWB, SWB);
+        const uint32_t acc = (kb | kk) != 0 ? 1u : 0u;
+        if constexpr (FMT == 2)
+          mma_tf32_ss_pair(tmem_base, adesc, bdesc, IDESC, acc);
+        else
+          mma_f16_ss_pair(tmem_base, adesc, bdesc, IDESC, acc);
+      }
+      mma_commit_pair(smem_u32(&sh.empty[s]));
+      mma_commit_pair(peer_empty0 + static_cast<uint32_t>(s) * 8u);
+    }
+    if (ok) {
+      mma_commit_pair(smem_u32(&sh.acc_full[0]));
+      mma_commit_pair(peer_acc);
+    } else {
+      mma_commit_pair(smem_u32(&sh.drain));
+      mbar_wait_drain(smem_u32(&sh.drain), 0, err);
+    }
+  }
+
+  // ------------------------------------------------------- epilogue (both)
+  __syncwarp();
+  {
+    const int q = warp & 3;
+    if (mbar_wait(smem_u32(&sh.acc_full[0]), 0, abort_flag, err, kErrWaitEpilogue)) {
+      tc_fence_after();
+      const int row = pm * 256 + static_cast<int>(rank) * 128 + q * 32 + lane;
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; ++c) {
+        uint32_t r[32];
+        tmem_ld32(tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(c * 32),
+                  r);
+        tmem_wait_ld();
+        const int col0 = pn * BN + c * 32;
+        if (row < M) {
+          T* dst = C + static_cast<int64_t>(row) * N + col0;
+          if (col0 + 32 <= N) {
+            if constexpr (ES == 2) {
+              uint32_t pk[16];
+#pragma unroll
+              for (int i = 0; i < 16; ++i) {
+                const float lo = __uint_as_float(r[2 * i]), hi = __uint_as_float(r[2 * i + 1]);
+                pk[i] = (FMT == 1) ? pack_bf16(lo, hi) : pack_f16(lo, hi);
+              }
+              uint4* d4 = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+              for (int i = 0; i < 4; ++i)
+                d4[i] = make_uint4(pk[4 * i], pk[4 * i + 1], pk[4 * i + 2], pk[4 * i + 3]);
+            } else {
+              uint4* d4 = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+              for (int i = 0; i < 8; ++i)
+                d4[i] = make_uint4(r[4 * i], r[4 * i + 1], r[4 * i + 2], r[4 * i + 3]);
+            }
+          } else {
+#pragma unroll
+            for (int i = 0; i < 32; ++i)
+              if (col0 + i < N) dst[i] = Elem<T>::from_f(__uint_as_float(r[i]));
+          }
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync_all();  // no CTA leaves while its peer may still signal it
+  tc_fence_after();
+  if (warp == 0) tmem_dealloc_pair(tmem_base, ALLOC);
+}
+
 // ------------------------------------------------------------------- host
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
@@ -341,6 +539,45 @@ gpo_status plan_matmul_tc(const gpo_key& k, Plan& p, std::string& log) {
     return GPO_BAD_CONFIG;
   }
   const bool persistent = k.num_warps == 8;
+  // BLOCK_M 256 with 4 warps: a CTA pair (cta_group::2), each CTA staging
+  // 128 rows of A and BLOCK_N/2 columns of B.  tf32 needs the 128-byte B
+  // chunk (BLOCK_N/2 * 4 >= 128) for its 32-bit MN-major layout.
+  const bool pair = BM == 256 && k.num_warps == 4 && (k.dtype != GPO_TF32 || BN >= 64);
+  if (pair) {
+    const uint32_t pa = 128u * BK * es, pb = static_cast<uint32_t>(BK) * (BN / 2) * es;
+    const uint32_t pst = (pa + pb + 1023u) & ~1023u;
+    int pc = 32;
+    while (pc < BN) pc *= 2;
+    // Never let more CTAs share an SM than its 512 TMEM columns hold: a pair
+    // allocation that had to wait on one SM of the pair while holding the
+    // other could otherwise wait on a second pair doing the opposite.  The
+    // shared-memory request is padded so that at most 512 / columns CTAs fit.
+    const uint32_t max_ctas = 512u / static_cast<uint32_t>(pc);
+    uint32_t pdyn = pst * static_cast<uint32_t>(k.num_stages) + 1024u;
+    pdyn = std::max<uint32_t>(pdyn, 233472u / (max_ctas + 1u) + 64u);
+    const uint32_t psmem = pdyn + static_cast<uint32_t>(sizeof(TcShared));
+    if (psmem > kMaxSmemPerCta) {
+      log = "shared memory " + std::to_string(psmem) + " B per CTA of the pair (" +
+            std::to_string(k.num_stages) + " stages x " + std::to_string(pst) +
+            " B) exceeds the 232448 B per-CTA limit";
+      return GPO_COMPILE_ERROR;
+    }
+    p.aux[0] = std::min(BK * es, 128);
+    p.aux[1] = static_cast<int>(pdyn);
+    p.aux[2] = 0;
+    p.aux[3] = 1;  // pair
+    p.family = "matmul_tc";
+    p.res.smem_bytes = psmem;
+    p.res.tmem_cols = static_cast<uint32_t>(pc);
+    p.res.threads_per_cta = 128u;
+    p.res.grid_x = static_cast<uint32_t>(2 * cdiv(M, 256) * cdiv(N, BN));
+    p.res.grid_y = p.res.grid_z = 1;
+    p.res.launches_per_call = 1;
+    const char* tn = k.dtype == GPO_BFLOAT16 ? "bf16" : k.dtype == GPO_FLOAT16 ? "f16" : "tf32";
+    snprintf(p.res.kernel, sizeof(p.res.kernel), "matmul_tc2_kernel<%s,256,%d,cta_pair>", tn, BN);
+    return GPO_OK;
+  }
+  p.aux[3] = 0;
   const uint32_t a_bytes = static_cast<uint32_t>(BM) * BK * es;
   const uint32_t b_bytes = static_cast<uint32_t>(BK) * BN * es;
   const uint32_t stage = (a_bytes + b_bytes + 1023u) & ~1023u;
@@ -402,6 +639,41 @@ static gpo_status run_tc(const gpo_key& k, const Plan& p, const gpo_args& a, con
   return launch_status();
 }
 
+template <typename T, int FMT, int BN>
+static gpo_status run_tc2(const gpo_key& k, const Plan& p, const gpo_args& a, const LaunchCtx& c,
+                          CUtensorMapDataType dt) {
+  const int es = sizeof(T);
+  const int64_t M = k.shape[0], N = k.shape[1], K = k.shape[2];
+  const int swa = p.aux[0];
+  constexpr int BNH = BN / 2;
+  constexpr int SWB = (BNH * sizeof(T)) < 128 ? (BNH * sizeof(T)) : 128;
+  CUtensorMap ma, mb;
+  if (!encode_2d(&ma, dt, a.in[0], M, K, es, swa / es, 128, swa)) return GPO_LAUNCH_ERROR;
+  if (!encode_2d(&mb, dt, a.in[1], K, N, es, SWB / es, k.block_k, SWB, FMT == 2))
+    return GPO_LAUNCH_ERROR;
+  auto kern = matmul_tc2_kernel<T, FMT, BN>;
+  const uint32_t dyn = static_cast<uint32_t>(p.aux[1]);
+  gpo_status s = ensure_smem_attr(reinterpret_cast<const void*>(kern), dyn);
+  if (s != GPO_OK) return s;
+  const unsigned grid = static_cast<unsigned>(2 * cdiv(M, 256) * cdiv(N, BN));
+  kern<<<grid, 128, dyn, c.stream>>>(ma, mb, static_cast<T*>(a.out), static_cast<int>(M),
+                                     static_cast<int>(N), static_cast<int>(K), k.block_k,
+                                     k.num_stages, k.group_m, swa, c.err);
+  return launch_status();
+}
+
+template <typename T, int FMT>
+static gpo_status run_tc2_bn(const gpo_key& k, const Plan& p, const gpo_args& a,
+                             const LaunchCtx& c, CUtensorMapDataType dt) {
+  switch (k.block_n) {
+    case 32: return run_tc2<T, FMT, 32>(k, p, a, c, dt);
+    case 64: return run_tc2<T, FMT, 64>(k, p, a, c, dt);
+    case 128: return run_tc2<T, FMT, 128>(k, p, a, c, dt);
+    case 256: return run_tc2<T, FMT, 256>(k, p, a, c, dt);
+    default: return GPO_INTERNAL;
+  }
+}
+
 template <typename T, int FMT, int BM, bool P>
 static gpo_status run_tc_bn(const gpo_key& k, const Plan& p, const gpo_args& a,
                             const LaunchCtx& c, CUtensorMapDataType dt) {
@@ -417,6 +689,7 @@ static gpo_status run_tc_bn(const gpo_key& k, const Plan& p, const gpo_args& a,
 template <typename T, int FMT>
 static gpo_status run_tc_dt(const gpo_key& k, const Plan& p, const gpo_args& a,
                             const LaunchCtx& c, CUtensorMapDataType dt) {
+  if (p.aux[3]) return run_tc2_bn<T, FMT>(k, p, a, c, dt);
   const bool P = p.aux[2] != 0;
   if (k.block_m == 128)
     return P ? run_tc_bn<T, FMT, 128, true>(k, p, a, c, dt)

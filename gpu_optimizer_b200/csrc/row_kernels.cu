@@ -9,6 +9,8 @@
 //   BLOCK_N <  N : online / two-pass — statistics pass over BLOCK_N tiles,
 //                  then a normalise pass that re-reads the row (which on
 //                  B200 mostly hits the 126 MB L2).
+// With num_stages >= 2 a single-tile row kernel runs persistent, prefetching
+// its next row while it reduces the current one (rows_pipe).
 // Thread t owns V consecutive elements (one 16-byte vector) per vector slot
 // and slots are strided by the CTA width, so every warp access is a
 // contiguous 512-byte segment.  Statistics are fp32.
@@ -102,6 +104,33 @@ __device__ __forceinline__ void row_store(T* __restrict__ row, int64_t n, int64_
   }
 }
 
+// exp(x - m) as 2^((x - m) * log2 e): one FFMA + one MUFU ex2 per element
+// (x = -inf gives 0).  neg_m_log2e = -m * log2(e).
+__device__ __forceinline__ float exp_shifted(float x, float neg_m_log2e) {
+  return ex2_approx(fmaf(x, 1.4426950408889634f, neg_m_log2e));
+}
+
+// Max / sum of a register array with 8 independent accumulators.
+template <int N>
+__device__ __forceinline__ float tree_max(const float (&v)[N]) {
+  float a[8];
+#pragma unroll
+  for (int t = 0; t < 8; ++t) a[t] = t < N ? v[t] : -INFINITY;
+#pragma unroll
+  for (int i = 8; i < N; ++i) a[i & 7] = fmaxf(a[i & 7], v[i]);
+  return fmaxf(fmaxf(fmaxf(a[0], a[1]), fmaxf(a[2], a[3])),
+               fmaxf(fmaxf(a[4], a[5]), fmaxf(a[6], a[7])));
+}
+template <int N>
+__device__ __forceinline__ float tree_sum(const float (&v)[N]) {
+  float a[8];
+#pragma unroll
+  for (int t = 0; t < 8; ++t) a[t] = t < N ? v[t] : 0.f;
+#pragma unroll
+  for (int i = 8; i < N; ++i) a[i & 7] += v[i];
+  return ((a[0] + a[1]) + (a[2] + a[3])) + ((a[4] + a[5]) + (a[6] + a[7]));
+}
+
 // Block reductions; every thread receives the result.
 __device__ __forceinline__ float block_allreduce_max(float v, float* red) {
   v = warp_max(v);
@@ -135,19 +164,13 @@ __global__ void __launch_bounds__(1024) softmax_tile_regs(const T* __restrict__ 
   T* yr = y + static_cast<int64_t>(blockIdx.x) * n;
   float v[VPT * V];
   row_load<T, VPT>(xr, n, 0, bn, vec, -INFINITY, v);
-  float m = -INFINITY;
+  const float m = block_allreduce_max(tree_max(v), red);
+  const float nm = -m * 1.4426950408889634f;
 #pragma unroll
-  for (int i = 0; i < VPT * V; ++i) m = fmaxf(m, v[i]);
-  m = block_allreduce_max(m, red);
-  float s = 0.f;
+  for (int i = 0; i < VPT * V; ++i) v[i] = exp_shifted(v[i], nm);  // masked slots -> 0
+  const float inv = 1.0f / block_allreduce_sum(tree_sum(v), red);
 #pragma unroll
-  for (int i = 0; i < VPT * V; ++i) {
-    v[i] = expf(v[i] - m);  // exp(-inf) = 0 for masked slots
-    s += v[i];
-  }
-  s = block_allreduce_sum(s, red);
-#pragma unroll
-  for (int i = 0; i < VPT * V; ++i) v[i] = v[i] / s;
+  for (int i = 0; i < VPT * V; ++i) v[i] *= inv;
   row_store<T, VPT>(yr, n, 0, bn, vec, v);
 }
 
@@ -170,12 +193,12 @@ __global__ void __launch_bounds__(1024) softmax_tile_smem(const T* __restrict__ 
   m = block_allreduce_max(m, red);
   float s = 0.f;
   for (int64_t i = threadIdx.x; i < n; i += blockDim.x) {
-    const float e = expf(srow[i] - m);
+    const float e = exp_shifted(srow[i], -m * 1.4426950408889634f);
     srow[i] = e;
     s += e;
   }
-  s = block_allreduce_sum(s, red);
-  for (int64_t i = threadIdx.x; i < n; i += blockDim.x) yr[i] = E::from_f(srow[i] / s);
+  const float inv = 1.0f / block_allreduce_sum(s, red);
+  for (int64_t i = threadIdx.x; i < n; i += blockDim.x) yr[i] = E::from_f(srow[i] * inv);
 }
 
 // Online two-pass softmax over BLOCK_N tiles (kernels.py:121-136): running
@@ -199,17 +222,19 @@ __global__ void __launch_bounds__(1024) softmax_online(const T* __restrict__ x,
     if (nm != -INFINITY) {
       float ts = 0.f;
 #pragma unroll
-      for (int i = 0; i < VPT * V; ++i) ts += expf(v[i] - nm);
-      s = s * expf(m - nm) + ts;
+      for (int i = 0; i < VPT * V; ++i) ts += exp_shifted(v[i], -nm * 1.4426950408889634f);
+      s = s * exp_shifted(m, -nm * 1.4426950408889634f) + ts;
       m = nm;
     }
   }
   const float M = block_allreduce_max(m, red);
-  const float S = block_allreduce_sum(m == -INFINITY ? 0.f : s * expf(m - M), red);
+  const float S = block_allreduce_sum(
+      m == -INFINITY ? 0.f : s * exp_shifted(m, -M * 1.4426950408889634f), red);
+  const float invS = 1.0f / S, nM = -M * 1.4426950408889634f;
   for (int64_t t0 = 0; t0 < n; t0 += bn) {
     row_load<T, VPT>(xr, n, t0, bn, vec, -INFINITY, v);
 #pragma unroll
-    for (int i = 0; i < VPT * V; ++i) v[i] = expf(v[i] - M) / S;
+    for (int i = 0; i < VPT * V; ++i) v[i] = exp_shifted(v[i], nM) * invS;
     row_store<T, VPT>(yr, n, t0, bn, vec, v);
   }
 }
@@ -229,21 +254,18 @@ __global__ void __launch_bounds__(1024) layernorm_tile_regs(const T* __restrict_
   T* yr = y + static_cast<int64_t>(blockIdx.x) * n;
   float v[VPT * V];
   row_load<T, VPT>(xr, n, 0, bn, vec, 0.f, v);
-  float s = 0.f;
-#pragma unroll
-  for (int i = 0; i < VPT * V; ++i) s += v[i];
-  const float mean = block_allreduce_sum(s, red) / static_cast<float>(n);
-  float q = 0.f;
+  const float mean = block_allreduce_sum(tree_sum(v), red) / static_cast<float>(n);
+  float dq[VPT * V];
 #pragma unroll
   for (int j = 0; j < VPT; ++j) {
     const int64_t e0 = (threadIdx.x + static_cast<int64_t>(j) * blockDim.x) * V;
 #pragma unroll
     for (int u = 0; u < V; ++u) {
       const float d = (e0 + u < n) ? v[j * V + u] - mean : 0.f;
-      q += d * d;
+      dq[j * V + u] = d * d;
     }
   }
-  const float var = block_allreduce_sum(q, red) / static_cast<float>(n);
+  const float var = block_allreduce_sum(tree_sum(dq), red) / static_cast<float>(n);
   const float rstd = 1.0f / sqrtf(var + eps);
   ln_affine<T, VPT>(w, b, n, 0, bn, vec, mean, rstd, v);
   row_store<T, VPT>(yr, n, 0, bn, vec, v);
@@ -312,6 +334,123 @@ __global__ void __launch_bounds__(1024) layernorm_twopass(const T* __restrict__ 
   }
 }
 
+// ------------------------------------------------- persistent, pipelined
+// num_stages >= 2 with a single register tile and 16-byte aligned rows:
+// gridDim.x persistent CTAs (SM count x resident CTAs) walk rows
+// blockIdx.x, blockIdx.x + gridDim.x, ...; while a CTA reduces and writes
+// row r it already has the raw 16-byte vectors of its next row in flight,
+// so HBM reads never wait on the block reductions.
+
+// Raw vector slots of one row (vec path: n*sizeof(T) % 16 == 0, so a slot
+// is either fully inside the row or fully outside; outside slots read 0).
+template <typename T, int VPT>
+__device__ __forceinline__ void raw_row_load(const T* __restrict__ row, int64_t n,
+                                             uint4 (&r)[VPT]) {
+  constexpr int V = RowVec<T>::V;
+#pragma unroll
+  for (int j = 0; j < VPT; ++j) {
+    const int64_t e0 = (threadIdx.x + static_cast<int64_t>(j) * blockDim.x) * V;
+    r[j] = e0 < n ? __ldcs(reinterpret_cast<const uint4*>(row + e0)) : make_uint4(0, 0, 0, 0);
+  }
+}
+
+template <typename T, int VPT>
+__device__ __forceinline__ void raw_unpack(const uint4 (&r)[VPT], int64_t n, float fill,
+                                           float (&v)[VPT * RowVec<T>::V]) {
+  using E = Elem<T>;
+  constexpr int V = RowVec<T>::V;
+#pragma unroll
+  for (int j = 0; j < VPT; ++j) {
+    const bool in = (threadIdx.x + static_cast<int64_t>(j) * blockDim.x) * V < n;
+    const T* e = reinterpret_cast<const T*>(&r[j]);
+#pragma unroll
+    for (int u = 0; u < V; ++u) v[j * V + u] = in ? E::to_f(e[u]) : fill;
+  }
+}
+
+template <typename T, int VPT>
+__device__ __forceinline__ void raw_row_store(T* __restrict__ row, int64_t n,
+                                              const float (&v)[VPT * RowVec<T>::V]) {
+  using E = Elem<T>;
+  constexpr int V = RowVec<T>::V;
+#pragma unroll
+  for (int j = 0; j < VPT; ++j) {
+    const int64_t e0 = (threadIdx.x + static_cast<int64_t>(j) * blockDim.x) * V;
+    if (e0 < n) {
+      uint4 r;
+      T* e = reinterpret_cast<T*>(&r);
+#pragma unroll
+      for (int u = 0; u < V; ++u) e[u] = E::from_f(v[j * V + u]);
+      __stcs(reinterpret_cast<uint4*>(row + e0), r);
+    }
+  }
+}
+
+template <typename T, int VPT>
+__global__ void __launch_bounds__(1024) softmax_rows_pipe(const T* __restrict__ x,
+                                                          T* __restrict__ y, int64_t m,
+                                                          int64_t n) {
+  constexpr int V = RowVec<T>::V;
+  __shared__ float red[32];
+  int64_t row = blockIdx.x;
+  if (row >= m) return;
+  uint4 cur[VPT], nxt[VPT];
+  raw_row_load<T, VPT>(x + row * n, n, cur);
+  for (; row < m; row += gridDim.x) {
+    const int64_t nr = row + gridDim.x;
+    if (nr < m) raw_row_load<T, VPT>(x + nr * n, n, nxt);
+    float v[VPT * V];
+    raw_unpack<T, VPT>(cur, n, -INFINITY, v);
+    const float mx = block_allreduce_max(tree_max(v), red);
+    const float nm = -mx * 1.4426950408889634f;
+#pragma unroll
+    for (int i = 0; i < VPT * V; ++i) v[i] = exp_shifted(v[i], nm);
+    const float inv = 1.0f / block_allreduce_sum(tree_sum(v), red);
+#pragma unroll
+    for (int i = 0; i < VPT * V; ++i) v[i] *= inv;
+    raw_row_store<T, VPT>(y + row * n, n, v);
+#pragma unroll
+    for (int j = 0; j < VPT; ++j) cur[j] = nxt[j];
+  }
+}
+
+template <typename T, int VPT>
+__global__ void __launch_bounds__(1024) layernorm_rows_pipe(const T* __restrict__ x,
+                                                            const T* __restrict__ w,
+                                                            const T* __restrict__ b,
+                                                            T* __restrict__ y, int64_t m,
+                                                            int64_t n, float eps) {
+  constexpr int V = RowVec<T>::V;
+  __shared__ float red[32];
+  int64_t row = blockIdx.x;
+  if (row >= m) return;
+  uint4 cur[VPT], nxt[VPT];
+  raw_row_load<T, VPT>(x + row * n, n, cur);
+  for (; row < m; row += gridDim.x) {
+    const int64_t nr = row + gridDim.x;
+    if (nr < m) raw_row_load<T, VPT>(x + nr * n, n, nxt);
+    float v[VPT * V];
+    raw_unpack<T, VPT>(cur, n, 0.f, v);
+    const float mean = block_allreduce_sum(tree_sum(v), red) / static_cast<float>(n);
+    float dq[VPT * V];
+#pragma unroll
+    for (int j = 0; j < VPT; ++j) {
+      const bool in = (threadIdx.x + static_cast<int64_t>(j) * blockDim.x) * V < n;
+#pragma unroll
+      for (int u = 0; u < V; ++u) {
+        const float d = in ? v[j * V + u] - mean : 0.f;
+        dq[j * V + u] = d * d;
+      }
+    }
+    const float var = block_allreduce_sum(tree_sum(dq), red) / static_cast<float>(n);
+    const float rstd = 1.0f / sqrtf(var + eps);
+    ln_affine<T, VPT>(w, b, n, 0, n, true, mean, rstd, v);
+    raw_row_store<T, VPT>(y + row * n, n, v);
+#pragma unroll
+    for (int j = 0; j < VPT; ++j) cur[j] = nxt[j];
+  }
+}
+
 // ------------------------------------------------------------------- host
 // Plan: aux[0] = VPT (vector slots per thread, 0 = smem-staged single tile),
 // aux[1] = single-tile flag, aux[2] = dynamic smem bytes.
@@ -355,6 +494,10 @@ static gpo_status plan_rows(const gpo_key& k, Plan& p, std::string& log, const c
   p.aux[0] = vpt;
   p.aux[1] = single ? 1 : 0;
   p.aux[2] = static_cast<int>(dyn);
+  // persistent row pipeline: register tile, single tile, aligned rows
+  const bool pipe = single && vpt > 0 && k.num_stages >= 2 &&
+                    (n * dtype_bytes(k.dtype)) % 16 == 0;
+  p.aux[3] = pipe ? 1 : 0;
   p.family = "row_kernels";
   p.res.threads_per_cta = static_cast<uint32_t>(threads);
   p.res.grid_x = static_cast<uint32_t>(std::max<int64_t>(1, k.shape[0]));
@@ -362,8 +505,11 @@ static gpo_status plan_rows(const gpo_key& k, Plan& p, std::string& log, const c
   p.res.launches_per_call = 1;
   p.res.smem_bytes = dyn + 128;
   snprintf(p.res.kernel, sizeof(p.res.kernel), "%s_%s<vpt=%d>", what,
-           single ? (vpt ? "tile_regs" : "tile_smem") : (k.task == GPO_TASK_SOFTMAX ? "online" : "twopass"),
+           pipe ? "rows_pipe"
+                : single ? (vpt ? "tile_regs" : "tile_smem")
+                         : (k.task == GPO_TASK_SOFTMAX ? "online" : "twopass"),
            vpt);
+  if (pipe) p.res.persistent = 1;
   return GPO_OK;
 }
 
@@ -381,7 +527,12 @@ static gpo_status softmax_vpt(const gpo_key& k, const Plan& p, const gpo_args& a
   const int threads = k.num_warps * 32;
   const T* x = static_cast<const T*>(a.in[0]);
   T* y = static_cast<T*>(a.out);
-  if (p.aux[1])
+  if (p.aux[3] && vec) {
+    auto kern = softmax_rows_pipe<T, VPT>;
+    const unsigned pg = persistent_grid(reinterpret_cast<const void*>(kern), threads, 0,
+                                        c.sm_count, k.shape[0]);
+    kern<<<pg, threads, 0, c.stream>>>(x, y, k.shape[0], k.shape[1]);
+  } else if (p.aux[1])
     softmax_tile_regs<T, VPT><<<grid, threads, 0, c.stream>>>(x, y, k.shape[1], k.block_n, vec);
   else
     softmax_online<T, VPT><<<grid, threads, 0, c.stream>>>(x, y, k.shape[1], k.block_n, vec);
@@ -433,7 +584,12 @@ static gpo_status layernorm_vpt(const gpo_key& k, const Plan& p, const gpo_args&
   const T* w = static_cast<const T*>(a.in[1]);
   const T* b = static_cast<const T*>(a.in[2]);
   T* y = static_cast<T*>(a.out);
-  if (p.aux[1])
+  if (p.aux[3] && vec) {
+    auto kern = layernorm_rows_pipe<T, VPT>;
+    const unsigned pg = persistent_grid(reinterpret_cast<const void*>(kern), threads, 0,
+                                        c.sm_count, k.shape[0]);
+    kern<<<pg, threads, 0, c.stream>>>(x, w, b, y, k.shape[0], k.shape[1], eps);
+  } else if (p.aux[1])
     layernorm_tile_regs<T, VPT>
         <<<grid, threads, 0, c.stream>>>(x, w, b, y, k.shape[1], k.block_n, eps, vec);
   else

@@ -132,3 +132,11 @@ def test_row_kernel_plans():
                                                 "num_stages": 1,
                                                 "dtype": "float32"}).resources()
     assert r["kernel"] == "layernorm_twopass<vpt=1>"
+
+
+def test_cta_pair_plan():
+    r = mm({"BLOCK_M": 256, "num_warps": 4, "num_stages": 3}).resources()
+    assert r["kernel"] == "matmul_tc2_kernel<bf16,256,256,cta_pair>"
+    assert r["grid"][0] == 2 * 16 * 16 and r["tmem_cols"] == 256
+    # padded so that at most 2 CTAs (2 x 256 TMEM columns) share an SM
+    assert 233472 // 3 < r["smem_bytes"] <= 227 * 1024
