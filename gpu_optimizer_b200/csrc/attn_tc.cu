@@ -20,7 +20,13 @@
 //           TMEM rescaled) when a block's max exceeds it by more than 8
 //           (a factor of 256); until then P <= 256, which 16-bit P and the
 //           fp32 accumulator represent exactly as well as P <= 1.
-// TMEM columns: O [0, D), S buffers [D, D+BN) and [D+BN, D+2BN).
+// num_warps 8 doubles the CTA: two softmax warpgroups (warps 4-7 and 8-11),
+// each owning its own 128-row query tile, share every K/V tile; the MMA
+// issuer interleaves S_A(j), S_B(j), PV_A(j-1), PV_B(j-1), so one group's
+// softmax overlaps the other's MMAs and each SM sub-partition runs two
+// softmax warps.
+// TMEM columns per tile t of NT: O_t [t*D, t*D+D), S_t buffers
+// [NT*D + (2t+b)*BN, +BN) for b in {0, 1}.
 #include <algorithm>
 
 #include "gpo_common.cuh"
@@ -31,15 +37,17 @@ namespace gpo {
 constexpr int kAttnMaxStages = 4;
 constexpr float kRescaleThreshold = 8.0f;
 
+constexpr int kAttnMaxTiles = 2;  // query tiles (softmax warpgroups) per CTA
+
 struct AttnShared {
   uint64_t q_full;
   uint64_t k_full[kAttnMaxStages];
   uint64_t v_full[kAttnMaxStages];
   uint64_t kv_empty[kAttnMaxStages];
-  uint64_t s_full[2];
-  uint64_t s_free[2];
-  uint64_t p_full[2];
-  uint64_t pv_done[2];
+  uint64_t s_full[kAttnMaxTiles][2];
+  uint64_t s_free[kAttnMaxTiles][2];
+  uint64_t p_full[kAttnMaxTiles][2];
+  uint64_t pv_done[kAttnMaxTiles][2];
   uint64_t drain;
   uint32_t tmem_base;
   int abort;
@@ -58,8 +66,8 @@ __device__ __forceinline__ uint32_t kmajor_swizzled(int row, int byte_in_row, in
   return off ^ (((off >> 7) & static_cast<uint32_t>(sw / 16 - 1)) << 4);
 }
 
-template <typename T, int FMT, int BN, int D, bool CAUSAL>
-__global__ void __launch_bounds__(256, 1)
+template <typename T, int FMT, int BN, int D, bool CAUSAL, int NT>
+__global__ void __launch_bounds__(NT == 1 ? 256 : 384, 1)
     attn_tc_kernel(const __grid_constant__ CUtensorMap tma_q,
                    const __grid_constant__ CUtensorMap tma_k,
                    const __grid_constant__ CUtensorMap tma_v, T* __restrict__ O, int S,
@@ -70,7 +78,7 @@ __global__ void __launch_bounds__(256, 1)
   constexpr uint32_t Q_BYTES = 128u * D * ES;
   constexpr uint32_t KV_BYTES = static_cast<uint32_t>(BN) * D * ES;
   constexpr uint32_t P_BYTES = 128u * BN * ES;
-  constexpr int COLS = D + 2 * BN;
+  constexpr int COLS = NT * D + NT * 2 * BN;
   constexpr int ALLOC = attn_tmem_alloc(COLS);
   constexpr uint32_t IDESC_S = make_idesc(FMT, 128, BN, false, false);
   constexpr uint32_t IDESC_O = make_idesc(FMT, 128, D, false, true);
@@ -78,23 +86,30 @@ __global__ void __launch_bounds__(256, 1)
   __shared__ AttnShared sh;
   extern __shared__ uint8_t dyn_smem[];
   const uint32_t base = (smem_u32(dyn_smem) + 1023u) & ~1023u;
-  const uint32_t q_smem = base;
-  const uint32_t p_smem = q_smem + Q_BYTES;                 // 2 buffers
-  const uint32_t kv_smem = p_smem + 2 * ((P_BYTES + 1023u) & ~1023u);
-  const uint32_t kv_stage = 2 * ((KV_BYTES + 1023u) & ~1023u);
+  const uint32_t q_smem = base;                             // NT tiles
   const uint32_t p_stride = (P_BYTES + 1023u) & ~1023u;
+  const uint32_t p_smem = q_smem + NT * Q_BYTES;            // NT x 2 buffers
+  const uint32_t kv_smem = p_smem + NT * 2 * p_stride;
+  const uint32_t kv_stage = 2 * ((KV_BYTES + 1023u) & ~1023u);
   const uint32_t v_off = (KV_BYTES + 1023u) & ~1023u;
   uint8_t* p_generic = dyn_smem + (p_smem - smem_u32(dyn_smem));
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int num_q_tiles = (S + 127) / 128;
+  constexpr int CTA_ROWS = 128 * NT;
+  const int num_q_tiles = (S + CTA_ROWS - 1) / CTA_ROWS;
   // longest causal rows first; identity order for the non-causal task
   const int qt = CAUSAL ? (num_q_tiles - 1 - static_cast<int>(blockIdx.x))
                         : static_cast<int>(blockIdx.x);
-  const int q0 = qt * 128;
+  const int q0 = qt * CTA_ROWS;
   const int bh = blockIdx.y;
-  const int kv_len = CAUSAL ? min(S, q0 + 128) : S;
-  const int nblk = (kv_len + BN - 1) / BN;
+  // KV blocks each query tile needs (causal tiles stop at their diagonal)
+  int nblk[NT];
+#pragma unroll
+  for (int t = 0; t < NT; ++t) {
+    const int kv_len = CAUSAL ? min(S, q0 + 128 * t + 128) : S;
+    nblk[t] = (kv_len + BN - 1) / BN;
+  }
+  const int nblk_max = nblk[NT - 1];
 
   if (threadIdx.x == 0) {
     mbar_init(smem_u32(&sh.q_full), 1);
@@ -103,12 +118,13 @@ __global__ void __launch_bounds__(256, 1)
       mbar_init(smem_u32(&sh.v_full[s]), 1);
       mbar_init(smem_u32(&sh.kv_empty[s]), 1);
     }
-    for (int b = 0; b < 2; ++b) {
-      mbar_init(smem_u32(&sh.s_full[b]), 1);
-      mbar_init(smem_u32(&sh.s_free[b]), 4);
-      mbar_init(smem_u32(&sh.p_full[b]), 4);
-      mbar_init(smem_u32(&sh.pv_done[b]), 1);
-    }
+    for (int t = 0; t < NT; ++t)
+      for (int b = 0; b < 2; ++b) {
+        mbar_init(smem_u32(&sh.s_full[t][b]), 1);
+        mbar_init(smem_u32(&sh.s_free[t][b]), 4);
+        mbar_init(smem_u32(&sh.p_full[t][b]), 4);
+        mbar_init(smem_u32(&sh.pv_done[t][b]), 1);
+      }
     mbar_init(smem_u32(&sh.drain), 1);
     sh.abort = 0;
     fence_barrier_init();
@@ -124,18 +140,20 @@ __global__ void __launch_bounds__(256, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = sh.tmem_base;
-  const uint32_t o_tmem = tmem;
   volatile int* abort_flag = &sh.abort;
 
   if (warp == 0 && lane == 0) {
     // ------------------------------------------------------------ producer
     bool ok = true;
     int issued = 0;
-    mbar_arrive_expect_tx(smem_u32(&sh.q_full), Q_BYTES);
+    mbar_arrive_expect_tx(smem_u32(&sh.q_full), NT * Q_BYTES);
 #pragma unroll
-    for (int a = 0; a < (D * ES) / SWQ; ++a)
-      tma_load_3d(q_smem + a * 128 * SWQ, &tma_q, smem_u32(&sh.q_full), a * (SWQ / ES), q0, bh);
-    for (int j = 0; j < nblk; ++j) {
+    for (int t = 0; t < NT; ++t)
+#pragma unroll
+      for (int a = 0; a < (D * ES) / SWQ; ++a)
+        tma_load_3d(q_smem + t * Q_BYTES + a * 128 * SWQ, &tma_q, smem_u32(&sh.q_full),
+                    a * (SWQ / ES), q0 + 128 * t, bh);
+    for (int j = 0; j < nblk_max; ++j) {
       const int s = j % stages;
       const uint32_t r = static_cast<uint32_t>(j / stages);
       if (!mbar_wait(smem_u32(&sh.kv_empty[s]), (r & 1u) ^ 1u, abort_flag, err,
@@ -167,81 +185,103 @@ __global__ void __launch_bounds__(256, 1)
   } else if (warp == 1 && lane == 0) {
     // ---------------------------------------------------------- MMA issuer
     bool ok = mbar_wait(smem_u32(&sh.q_full), 0, abort_flag, err, kErrWaitMma);
-    auto issue_pv = [&](int i) -> bool {
+    // O_t += P_t(i) V(i) for every tile that still needs block i, then
+    // release the K/V stage of block i.
+    auto pv_round = [&](int i) -> bool {
       const int s = i % stages;
       const uint32_t r = static_cast<uint32_t>(i / stages);
       const int b = i & 1;
       const uint32_t u = static_cast<uint32_t>(i >> 1);
-      if (!mbar_wait(smem_u32(&sh.p_full[b]), u & 1u, abort_flag, err, kErrWaitMma)) return false;
       if (!mbar_wait(smem_u32(&sh.v_full[s]), r & 1u, abort_flag, err, kErrWaitMma)) return false;
-      tc_fence_after();
-      const uint32_t pb = p_smem + b * p_stride;
       const uint32_t vs = kv_smem + s * kv_stage + v_off;
 #pragma unroll
-      for (int kk = 0; kk < BN / 16; ++kk) {
-        const uint32_t kbyte = static_cast<uint32_t>(kk) * 32u;
-        const uint64_t adesc =
-            make_smem_desc(pb + (kbyte / SWP) * (128 * SWP) + (kbyte % SWP), 16, 8 * SWP, SWP);
-        const uint64_t bdesc = make_smem_desc(vs + kk * 16 * SWQ, BN * SWQ, 8 * SWQ, SWQ);
-        mma_f16_ss(o_tmem, adesc, bdesc, IDESC_O, (i > 0 || kk > 0) ? 1u : 0u);
+      for (int t = 0; t < NT; ++t) {
+        if (i >= nblk[t]) continue;
+        if (!mbar_wait(smem_u32(&sh.p_full[t][b]), u & 1u, abort_flag, err, kErrWaitMma))
+          return false;
+        tc_fence_after();
+        const uint32_t pb = p_smem + (t * 2 + b) * p_stride;
+#pragma unroll
+        for (int kk = 0; kk < BN / 16; ++kk) {
+          const uint32_t kbyte = static_cast<uint32_t>(kk) * 32u;
+          const uint64_t adesc = make_smem_desc(pb + (kbyte / SWP) * (128 * SWP) + (kbyte % SWP),
+                                                16, 8 * SWP, SWP);
+          const uint64_t bdesc = make_smem_desc(vs + kk * 16 * SWQ, BN * SWQ, 8 * SWQ, SWQ);
+          mma_f16_ss(tmem + static_cast<uint32_t>(t * D), adesc, bdesc, IDESC_O,
+                     (i > 0 || kk > 0) ? 1u : 0u);
+        }
+        mma_commit(smem_u32(&sh.pv_done[t][b]));
       }
       mma_commit(smem_u32(&sh.kv_empty[s]));
-      mma_commit(smem_u32(&sh.pv_done[b]));
       return true;
     };
-    // With a single K/V stage, K_j can only land after PV_{j-1} frees the
-    // stage, so PV_{j-1} is issued before S_j instead of after it.
+    // With a single K/V stage, K_j can only land after block j-1's PV frees
+    // the stage, so that PV round is issued before S_j instead of after it.
     const bool pv_first = stages == 1;
-    for (int j = 0; j < nblk && ok; ++j) {
+    for (int j = 0; j < nblk_max && ok; ++j) {
       const int s = j % stages;
       const uint32_t r = static_cast<uint32_t>(j / stages);
       const int b = j & 1;
       const uint32_t u = static_cast<uint32_t>(j >> 1);
-      if (pv_first && j > 0 && !issue_pv(j - 1)) {
+      if (pv_first && j > 0 && !pv_round(j - 1)) {
         ok = false;
         break;
       }
-      if (!mbar_wait(smem_u32(&sh.k_full[s]), r & 1u, abort_flag, err, kErrWaitMma) ||
-          !mbar_wait(smem_u32(&sh.s_free[b]), (u & 1u) ^ 1u, abort_flag, err, kErrWaitMma)) {
+      if (!mbar_wait(smem_u32(&sh.k_full[s]), r & 1u, abort_flag, err, kErrWaitMma)) {
         ok = false;
         break;
       }
-      tc_fence_after();
       const uint32_t ks = kv_smem + s * kv_stage;
-      const uint32_t s_tmem = tmem + static_cast<uint32_t>(D + b * BN);
 #pragma unroll
-      for (int kk = 0; kk < D / 16; ++kk) {
-        const uint32_t kbyte = static_cast<uint32_t>(kk) * 32u;
-        const uint32_t aoff = (kbyte / SWQ) * (128 * SWQ) + (kbyte % SWQ);
-        const uint32_t boff = (kbyte / SWQ) * (BN * SWQ) + (kbyte % SWQ);
-        const uint64_t adesc = make_smem_desc(q_smem + aoff, 16, 8 * SWQ, SWQ);
-        const uint64_t bdesc = make_smem_desc(ks + boff, 16, 8 * SWQ, SWQ);
-        mma_f16_ss(s_tmem, adesc, bdesc, IDESC_S, kk > 0 ? 1u : 0u);
+      for (int t = 0; t < NT; ++t) {
+        if (j >= nblk[t]) continue;
+        if (!mbar_wait(smem_u32(&sh.s_free[t][b]), (u & 1u) ^ 1u, abort_flag, err,
+                       kErrWaitMma)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t s_tmem = tmem + static_cast<uint32_t>(NT * D + (t * 2 + b) * BN);
+        const uint32_t qs = q_smem + t * Q_BYTES;
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t kbyte = static_cast<uint32_t>(kk) * 32u;
+          const uint32_t aoff = (kbyte / SWQ) * (128 * SWQ) + (kbyte % SWQ);
+          const uint32_t boff = (kbyte / SWQ) * (BN * SWQ) + (kbyte % SWQ);
+          const uint64_t adesc = make_smem_desc(qs + aoff, 16, 8 * SWQ, SWQ);
+          const uint64_t bdesc = make_smem_desc(ks + boff, 16, 8 * SWQ, SWQ);
+          mma_f16_ss(s_tmem, adesc, bdesc, IDESC_S, kk > 0 ? 1u : 0u);
+        }
+        mma_commit(smem_u32(&sh.s_full[t][b]));
       }
-      mma_commit(smem_u32(&sh.s_full[b]));
-      if (!pv_first && j > 0 && !issue_pv(j - 1)) {
+      if (!ok) break;
+      if (!pv_first && j > 0 && !pv_round(j - 1)) {
         ok = false;
         break;
       }
     }
-    if (ok && nblk > 0) ok = issue_pv(nblk - 1);
+    if (ok && nblk_max > 0) ok = pv_round(nblk_max - 1);
     if (!ok) {
       mma_commit(smem_u32(&sh.drain));
       mbar_wait_drain(smem_u32(&sh.drain), 0, err);
     }
   } else if (warp >= 4) {
     // ------------------------------------------- softmax / correction / epilogue
-    const int q = warp & 3;
-    const int row = q * 32 + lane;  // query row within the tile == TMEM lane
-    const int qrow = q0 + row;
+    const int tile = (warp - 4) >> 2;  // query tile of this warpgroup
+    const int q = warp & 3;            // TMEM lane quarter of this warp
+    const int row = q * 32 + lane;     // query row within the tile == TMEM lane
+    const int tq0 = q0 + 128 * tile;
+    const int qrow = tq0 + row;
+    const int my_nblk = nblk[tile];
     const uint32_t lane_addr = static_cast<uint32_t>(q * 32) << 16;
+    const uint32_t o_tmem = tmem + static_cast<uint32_t>(tile * D);
     float m_used = -INFINITY;
     float l = 0.f;
     bool ok = true;
-    for (int j = 0; j < nblk; ++j) {
+    for (int j = 0; j < my_nblk; ++j) {
       const int b = j & 1;
       const uint32_t u = static_cast<uint32_t>(j >> 1);
-      if (!mbar_wait(smem_u32(&sh.s_full[b]), u & 1u, abort_flag, err, kErrWaitSoftmax)) {
+      if (!mbar_wait(smem_u32(&sh.s_full[tile][b]), u & 1u, abort_flag, err, kErrWaitSoftmax)) {
         ok = false;
         break;
       }
@@ -252,7 +292,7 @@ __global__ void __launch_bounds__(256, 1)
         uint32_t r[BN];
 #pragma unroll
         for (int c = 0; c < BN / 32; ++c)
-          tmem_ld32(tmem + lane_addr + static_cast<uint32_t>(D + b * BN + c * 32),
+          tmem_ld32(tmem + lane_addr + static_cast<uint32_t>(NT * D + (tile * 2 + b) * BN + c * 32),
                     *reinterpret_cast<uint32_t(*)[32]>(r + c * 32));
         tmem_wait_ld();
 #pragma unroll
@@ -260,13 +300,13 @@ __global__ void __launch_bounds__(256, 1)
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(smem_u32(&sh.s_free[b]));
+      if (lane == 0) mbar_arrive(smem_u32(&sh.s_free[tile][b]));
 
       // Mask padding / future keys only where the block needs it (block-
       // uniform test on the tile's first row); work on raw scores, with the
       // log2-domain scale folded into the exponent's FMA below.
       const int key0 = j * BN;
-      const bool need_mask = key0 + BN > S || (CAUSAL && key0 + BN - 1 > q0);
+      const bool need_mask = key0 + BN > S || (CAUSAL && key0 + BN - 1 > tq0);
       if (need_mask) {
 #pragma unroll
         for (int i = 0; i < BN; ++i) {
@@ -291,7 +331,7 @@ __global__ void __launch_bounds__(256, 1)
           const float alpha = ex2_approx(m_used - m_new);
           // O holds PV_0..PV_{j-1}; wait for PV_{j-1} before rescaling it
           const int pj = j - 1;
-          if (!mbar_wait(smem_u32(&sh.pv_done[pj & 1]), static_cast<uint32_t>(pj >> 1) & 1u,
+          if (!mbar_wait(smem_u32(&sh.pv_done[tile][pj & 1]), static_cast<uint32_t>(pj >> 1) & 1u,
                          abort_flag, err, kErrWaitSoftmax)) {
             ok = false;
             break;
@@ -323,13 +363,13 @@ __global__ void __launch_bounds__(256, 1)
       l += ((rs8[0] + rs8[1]) + (rs8[2] + rs8[3])) + ((rs8[4] + rs8[5]) + (rs8[6] + rs8[7]));
       if (j >= 2) {
         const int pj = j - 2;
-        if (!mbar_wait(smem_u32(&sh.pv_done[pj & 1]), static_cast<uint32_t>(pj >> 1) & 1u,
+        if (!mbar_wait(smem_u32(&sh.pv_done[tile][pj & 1]), static_cast<uint32_t>(pj >> 1) & 1u,
                        abort_flag, err, kErrWaitSoftmax)) {
           ok = false;
           break;
         }
       }
-      uint8_t* pbuf = p_generic + b * p_stride;
+      uint8_t* pbuf = p_generic + (tile * 2 + b) * p_stride;
 #pragma unroll
       for (int g = 0; g < BN / 8; ++g) {
         uint4 v4;
@@ -347,12 +387,12 @@ __global__ void __launch_bounds__(256, 1)
       fence_proxy_async_smem();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(smem_u32(&sh.p_full[b]));
+      if (lane == 0) mbar_arrive(smem_u32(&sh.p_full[tile][b]));
     }
     // ------------------------------------------------------------ epilogue
-    if (ok && nblk > 0) {
-      const int pj = nblk - 1;
-      ok = mbar_wait(smem_u32(&sh.pv_done[pj & 1]), static_cast<uint32_t>(pj >> 1) & 1u,
+    if (ok && my_nblk > 0) {
+      const int pj = my_nblk - 1;
+      ok = mbar_wait(smem_u32(&sh.pv_done[tile][pj & 1]), static_cast<uint32_t>(pj >> 1) & 1u,
                      abort_flag, err, kErrWaitSoftmax);
     }
     if (ok) {
@@ -410,50 +450,57 @@ static bool encode_bsd(CUtensorMap* map, CUtensorMapDataType dt, const void* ptr
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-static uint32_t attn_tc_smem(int BN, int D, int stages) {
+static uint32_t attn_tc_smem(int BN, int D, int stages, int nt) {
   auto al = [](uint32_t x) { return (x + 1023u) & ~1023u; };
   const uint32_t q = 128u * D * 2, p = 128u * BN * 2, kv = static_cast<uint32_t>(BN) * D * 2;
-  return al(q) + 2 * al(p) + static_cast<uint32_t>(stages) * 2 * al(kv) + 1024u;
+  return static_cast<uint32_t>(nt) * (al(q) + 2 * al(p)) +
+         static_cast<uint32_t>(stages) * 2 * al(kv) + 1024u;
 }
 
-// Plan: aux[0] = dynamic smem bytes.
+// Plan: aux[0] = dynamic smem bytes, aux[1] = query tiles per CTA (NT).
+// num_warps 4 -> one softmax warpgroup (NT = 1); 8 -> two (NT = 2).
 gpo_status plan_attention_tc(const gpo_key& k, Plan& p, std::string& log) {
   const int D = static_cast<int>(k.shape[2]);
   const int BN = k.block_n;
+  const int nt = k.num_warps == 8 ? 2 : 1;
   if (k.num_stages < 1 || k.num_stages > kAttnMaxStages) {
     log = "num_stages must be in [1, 4]";
     return GPO_BAD_CONFIG;
   }
-  const uint32_t dyn = attn_tc_smem(BN, D, k.num_stages);
-  const uint32_t smem = dyn + static_cast<uint32_t>(sizeof(AttnShared));
-  if (smem > kMaxSmemPerCta) {
-    log = "shared memory " + std::to_string(smem) + " B (Q, 2 P buffers, " +
-          std::to_string(k.num_stages) + " K/V stages) exceeds the 232448 B per-CTA limit";
+  const int cols_needed = nt * D + nt * 2 * BN;
+  if (cols_needed > static_cast<int>(kTmemCols)) {
+    log = "TMEM needs " + std::to_string(cols_needed) + " columns (" + std::to_string(nt) +
+          " query tiles x (O " + std::to_string(D) + " + 2 S buffers x " + std::to_string(BN) +
+          ")) > 512";
     return GPO_COMPILE_ERROR;
   }
-  const int cols = attn_tmem_alloc(D + 2 * BN);
-  if (D + 2 * BN > static_cast<int>(kTmemCols)) {
-    log = "TMEM needs " + std::to_string(D + 2 * BN) + " columns > 512";
+  const uint32_t dyn = attn_tc_smem(BN, D, k.num_stages, nt);
+  const uint32_t smem = dyn + static_cast<uint32_t>(sizeof(AttnShared));
+  if (smem > kMaxSmemPerCta) {
+    log = "shared memory " + std::to_string(smem) + " B (" + std::to_string(nt) +
+          " x (Q + 2 P buffers), " + std::to_string(k.num_stages) +
+          " K/V stages) exceeds the 232448 B per-CTA limit";
     return GPO_COMPILE_ERROR;
   }
   p.aux[0] = static_cast<int>(dyn);
+  p.aux[1] = nt;
   p.family = "attn_tc";
   p.res.smem_bytes = smem;
-  p.res.tmem_cols = static_cast<uint32_t>(cols);
-  p.res.threads_per_cta = 256;
-  p.res.grid_x = static_cast<uint32_t>(cdiv(k.shape[1], 128));
+  p.res.tmem_cols = static_cast<uint32_t>(attn_tmem_alloc(cols_needed));
+  p.res.threads_per_cta = nt == 2 ? 384u : 256u;
+  p.res.grid_x = static_cast<uint32_t>(cdiv(k.shape[1], 128 * nt));
   p.res.grid_y = static_cast<uint32_t>(k.shape[0]);
   p.res.grid_z = 1;
   p.res.launches_per_call = 1;
-  snprintf(p.res.kernel, sizeof(p.res.kernel), "attn_tc_kernel<%s,BN=%d,D=%d,%s>",
+  snprintf(p.res.kernel, sizeof(p.res.kernel), "attn_tc_kernel<%s,BN=%d,D=%d,%s,tiles=%d>",
            k.dtype == GPO_BFLOAT16 ? "bf16" : "f16", BN, D,
-           k.task == GPO_TASK_ATTENTION_CAUSAL ? "causal" : "full");
+           k.task == GPO_TASK_ATTENTION_CAUSAL ? "causal" : "full", nt);
   return GPO_OK;
 }
 
-template <typename T, int FMT, int BN, int D, bool CAUSAL>
-static gpo_status run_attn_tc(const gpo_key& k, const Plan& p, const gpo_args& a,
-                              const LaunchCtx& c, CUtensorMapDataType dt) {
+template <typename T, int FMT, int BN, int D, bool CAUSAL, int NT>
+static gpo_status run_attn_tc_nt(const gpo_key& k, const Plan& p, const gpo_args& a,
+                                 const LaunchCtx& c, CUtensorMapDataType dt) {
   const uint64_t BH = static_cast<uint64_t>(k.shape[0]), S = static_cast<uint64_t>(k.shape[1]);
   constexpr int SW = (D * 2) < 128 ? (D * 2) : 128;
   CUtensorMap mq, mk, mv;
@@ -461,15 +508,26 @@ static gpo_status run_attn_tc(const gpo_key& k, const Plan& p, const gpo_args& a
       !encode_bsd(&mk, dt, a.in[1], BH, S, D, BN, SW) ||
       !encode_bsd(&mv, dt, a.in[2], BH, S, D, BN, SW))
     return GPO_LAUNCH_ERROR;
-  auto kern = attn_tc_kernel<T, FMT, BN, D, CAUSAL>;
+  auto kern = attn_tc_kernel<T, FMT, BN, D, CAUSAL, NT>;
   const uint32_t dyn = static_cast<uint32_t>(p.aux[0]);
   gpo_status s = ensure_smem_attr(reinterpret_cast<const void*>(kern), dyn);
   if (s != GPO_OK) return s;
-  const dim3 grid(static_cast<unsigned>(cdiv(S, 128)), static_cast<unsigned>(BH));
+  const dim3 grid(static_cast<unsigned>(cdiv(S, 128 * NT)), static_cast<unsigned>(BH));
   const float scale_log2 = 1.4426950408889634f / sqrtf(static_cast<float>(D));
-  kern<<<grid, 256, dyn, c.stream>>>(mq, mk, mv, static_cast<T*>(a.out), static_cast<int>(S),
-                                     k.num_stages, scale_log2, c.err);
+  kern<<<grid, NT == 2 ? 384 : 256, dyn, c.stream>>>(mq, mk, mv, static_cast<T*>(a.out),
+                                                     static_cast<int>(S), k.num_stages,
+                                                     scale_log2, c.err);
   return launch_status();
+}
+
+template <typename T, int FMT, int BN, int D, bool CAUSAL>
+static gpo_status run_attn_tc(const gpo_key& k, const Plan& p, const gpo_args& a,
+                              const LaunchCtx& c, CUtensorMapDataType dt) {
+  if constexpr (2 * D + 4 * BN <= 512) {
+    if (p.aux[1] == 2) return run_attn_tc_nt<T, FMT, BN, D, CAUSAL, 2>(k, p, a, c, dt);
+  }
+  if (p.aux[1] != 1) return GPO_INTERNAL;
+  return run_attn_tc_nt<T, FMT, BN, D, CAUSAL, 1>(k, p, a, c, dt);
 }
 
 template <typename T, int FMT, int BN, bool CAUSAL>

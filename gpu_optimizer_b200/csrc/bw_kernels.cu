@@ -22,9 +22,31 @@ enum EwOp : int {
   kOpScale = 1,      // a * s                        (scale_kernel, kernels.py:195-201)
   kOpRelu = 2,       // max(a, 0)                    (relu_kernel, kernels.py:203-209)
   kOpFusedRelu = 3,  // max(a*s + b, 0) in fp32      (kernels.py:182-193)
-  kOpGelu = 4,       // gelu(a), erf form
+  kOpGelu = 4,       // gelu(a), erf form (erf per A&S 7.1.26)
   kOpFusedGelu = 5,  // gelu(a*s + b) in fp32
 };
+
+// erf(x) by Abramowitz & Stegun, Handbook of Mathematical Functions,
+// formula 7.1.26: erf(x) = 1 - (a1 t + a2 t^2 + a3 t^3 + a4 t^4 + a5 t^5)
+// exp(-x^2), t = 1 / (1 + p x), x >= 0, |error| <= 1.5e-7; odd extension
+// for x < 0.  One reciprocal, one exp2 and a 5-term Horner chain.
+__device__ __forceinline__ float erf_as7126(float x) {
+  const float ax = fabsf(x);
+  float t;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(t) : "f"(fmaf(0.3275911f, ax, 1.0f)));
+  float poly = fmaf(1.061405429f, t, -1.453152027f);
+  poly = fmaf(poly, t, 1.421413741f);
+  poly = fmaf(poly, t, -0.284496736f);
+  poly = fmaf(poly, t, 0.254829592f);
+  poly *= t;
+  const float e = ex2_approx(-ax * ax * 1.4426950408889634f);  // exp(-x^2)
+  return copysignf(fmaf(-poly, e, 1.0f), x);
+}
+
+// gelu(z) = z * Phi(z) = 0.5 z (1 + erf(z / sqrt 2))
+__device__ __forceinline__ float gelu_erf(float z) {
+  return 0.5f * z * (1.0f + erf_as7126(z * 0.70710678118654752f));
+}
 
 template <int OP>
 __device__ __forceinline__ float ew_apply(float a, float b, float s) {
@@ -39,10 +61,9 @@ __device__ __forceinline__ float ew_apply(float a, float b, float s) {
     const float z = __fadd_rn(__fmul_rn(a, s), b);
     return z > 0.f ? z : 0.f;
   } else if constexpr (OP == kOpGelu) {
-    return 0.5f * a * (1.0f + erff(a * 0.70710678118654752f));
+    return gelu_erf(a);
   } else {
-    const float z = __fadd_rn(__fmul_rn(a, s), b);
-    return 0.5f * z * (1.0f + erff(z * 0.70710678118654752f));
+    return gelu_erf(__fadd_rn(__fmul_rn(a, s), b));
   }
 }
 

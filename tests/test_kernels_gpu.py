@@ -88,8 +88,9 @@ def task_configs(name, dtype):
                  "dtype": dtype} for bm, bn, w, s in ((32, 32, 4, 1), (16, 64, 2, 2),
                                                       (64, 32, 8, 2))]
         if dtype != "float32":
-            cfgs += [{"BLOCK_M": 128, "BLOCK_N": bn, "num_warps": 4, "num_stages": s,
-                      "dtype": dtype} for bn, s in ((32, 1), (64, 2), (128, 2), (32, 4))]
+            cfgs += [{"BLOCK_M": 128, "BLOCK_N": bn, "num_warps": w, "num_stages": s,
+                      "dtype": dtype} for bn, s, w in ((32, 1, 4), (64, 2, 4), (128, 2, 4),
+                                                       (32, 4, 4), (64, 2, 8), (32, 3, 8))]
         return cfgs
     raise KeyError(name)
 
@@ -175,9 +176,10 @@ def test_tcgen05_attention_shapes(shape, dtype, causal):
     inputs = O.make_inputs(name, shape, dtype, 2)
     ref = O.reference(name, inputs)
     ran = 0
-    for bn in (32, 64, 128):
-        for stages in (1, 2, 3):
-            cfg = {"BLOCK_M": 128, "BLOCK_N": bn, "num_warps": 4, "num_stages": stages,
+    for bn, stages, warps in [(bn, st, w) for bn in (32, 64, 128) for st in (1, 2, 3)
+                              for w in (4, 8)]:
+        if True:
+            cfg = {"BLOCK_M": 128, "BLOCK_N": bn, "num_warps": warps, "num_stages": stages,
                    "dtype": dtype}
             try:
                 out, kc = run(name, shape, cfg, inputs)
