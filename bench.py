@@ -369,7 +369,7 @@ EXTRA_TASKS = [
     ("fused_gelu", (1 << 26,), {"BLOCK_SIZE": 4096, "num_warps": 8, "strategy": "fused",
                                 "dtype": "bfloat16"}),
     ("attention_causal", (128, 4096, 128), {"BLOCK_M": 128, "BLOCK_N": 128, "num_warps": 4,
-                                            "num_stages": 2, "dtype": "bfloat16"}),
+                                            "num_stages": 3, "dtype": "bfloat16"}),
     ("matmul", (8192, 8192, 8192), {"BLOCK_M": 256, "BLOCK_N": 256, "BLOCK_K": 64,
                                     "GROUP_M": 16, "num_warps": 4, "num_stages": 3,
                                     "dtype": "bfloat16"}),

@@ -14,9 +14,9 @@
 //   warps 4-7 softmax / correction / epilogue: thread r owns query row r
 //           (TMEM lane r).  It reads S_j from TMEM, applies scale, padding
 //           and causal masks, keeps the running max in the log2 domain,
-//           writes P_j = exp2(s - m) as 16-bit values into a swizzled shared
-//           buffer (the A operand of the PV MMA) and accumulates the fp32
-//           row sum.  The running max used for P is only moved (and O in
+//           writes P_j = exp2(s - m) as 16-bit pairs back into TMEM over its
+//           own S buffer (the A operand of the PV MMA, read from TMEM) and
+//           accumulates the fp32 row sum.  The running max used for P is only moved (and O in
 //           TMEM rescaled) when a block's max exceeds it by more than 8
 //           (a factor of 256); until then P <= 256, which 16-bit P and the
 //           fp32 accumulator represent exactly as well as P <= 1.
@@ -57,15 +57,6 @@ __host__ __device__ constexpr int attn_tmem_alloc(int cols) {
   return cols <= 32 ? 32 : cols <= 64 ? 64 : cols <= 128 ? 128 : cols <= 256 ? 256 : 512;
 }
 
-// Byte offset of 16-byte chunk `chunk` of row `row` inside a K-major
-// swizzled tile of 128 rows whose rows are split into atoms of `sw` bytes.
-__device__ __forceinline__ uint32_t kmajor_swizzled(int row, int byte_in_row, int sw) {
-  const uint32_t atom = static_cast<uint32_t>(byte_in_row / sw);
-  const uint32_t off = atom * (128u * sw) + static_cast<uint32_t>(row) * sw +
-                       static_cast<uint32_t>(byte_in_row % sw);
-  return off ^ (((off >> 7) & static_cast<uint32_t>(sw / 16 - 1)) << 4);
-}
-
 template <typename T, int FMT, int BN, int D, bool CAUSAL, int NT>
 __global__ void __launch_bounds__(NT == 1 ? 256 : 384, 1)
     attn_tc_kernel(const __grid_constant__ CUtensorMap tma_q,
@@ -74,10 +65,8 @@ __global__ void __launch_bounds__(NT == 1 ? 256 : 384, 1)
                    int stages, float scale_log2, unsigned int* err) {
   constexpr int ES = 2;
   constexpr int SWQ = (D * ES) < 128 ? (D * ES) : 128;  // swizzle of Q/K/V rows
-  constexpr int SWP = (BN * ES) < 128 ? (BN * ES) : 128;  // swizzle of P rows
   constexpr uint32_t Q_BYTES = 128u * D * ES;
   constexpr uint32_t KV_BYTES = static_cast<uint32_t>(BN) * D * ES;
-  constexpr uint32_t P_BYTES = 128u * BN * ES;
   constexpr int COLS = NT * D + NT * 2 * BN;
   constexpr int ALLOC = attn_tmem_alloc(COLS);
   constexpr uint32_t IDESC_S = make_idesc(FMT, 128, BN, false, false);
@@ -87,12 +76,9 @@ __global__ void __launch_bounds__(NT == 1 ? 256 : 384, 1)
   extern __shared__ uint8_t dyn_smem[];
   const uint32_t base = (smem_u32(dyn_smem) + 1023u) & ~1023u;
   const uint32_t q_smem = base;                             // NT tiles
-  const uint32_t p_stride = (P_BYTES + 1023u) & ~1023u;
-  const uint32_t p_smem = q_smem + NT * Q_BYTES;            // NT x 2 buffers
-  const uint32_t kv_smem = p_smem + NT * 2 * p_stride;
+  const uint32_t kv_smem = q_smem + NT * Q_BYTES;
   const uint32_t kv_stage = 2 * ((KV_BYTES + 1023u) & ~1023u);
   const uint32_t v_off = (KV_BYTES + 1023u) & ~1023u;
-  uint8_t* p_generic = dyn_smem + (p_smem - smem_u32(dyn_smem));
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   constexpr int CTA_ROWS = 128 * NT;
@@ -102,14 +88,13 @@ __global__ void __launch_bounds__(NT == 1 ? 256 : 384, 1)
                         : static_cast<int>(blockIdx.x);
   const int q0 = qt * CTA_ROWS;
   const int bh = blockIdx.y;
-  // KV blocks each query tile needs (causal tiles stop at their diagonal)
-  int nblk[NT];
-#pragma unroll
-  for (int t = 0; t < NT; ++t) {
+  // KV blocks query tile t needs (causal tiles stop at their diagonal);
+  // computed, not indexed from an array, so it never lands in local memory
+  auto nblk_of = [&](int t) -> int {
     const int kv_len = CAUSAL ? min(S, q0 + 128 * t + 128) : S;
-    nblk[t] = (kv_len + BN - 1) / BN;
-  }
-  const int nblk_max = nblk[NT - 1];
+    return (kv_len + BN - 1) / BN;
+  };
+  const int nblk_max = nblk_of(NT - 1);
 
   if (threadIdx.x == 0) {
     mbar_init(smem_u32(&sh.q_full), 1);
@@ -196,19 +181,17 @@ __global__ void __launch_bounds__(NT == 1 ? 256 : 384, 1)
       const uint32_t vs = kv_smem + s * kv_stage + v_off;
 #pragma unroll
       for (int t = 0; t < NT; ++t) {
-        if (i >= nblk[t]) continue;
+        if (i >= nblk_of(t)) continue;
         if (!mbar_wait(smem_u32(&sh.p_full[t][b]), u & 1u, abort_flag, err, kErrWaitMma))
           return false;
         tc_fence_after();
-        const uint32_t pb = p_smem + (t * 2 + b) * p_stride;
+        // P_t(i) sits in the first BN/2 columns of S buffer b (16-bit pairs)
+        const uint32_t pa = tmem + static_cast<uint32_t>(NT * D + (t * 2 + b) * BN);
 #pragma unroll
         for (int kk = 0; kk < BN / 16; ++kk) {
-          const uint32_t kbyte = static_cast<uint32_t>(kk) * 32u;
-          const uint64_t adesc = make_smem_desc(pb + (kbyte / SWP) * (128 * SWP) + (kbyte % SWP),
-                                                16, 8 * SWP, SWP);
           const uint64_t bdesc = make_smem_desc(vs + kk * 16 * SWQ, BN * SWQ, 8 * SWQ, SWQ);
-          mma_f16_ss(tmem + static_cast<uint32_t>(t * D), adesc, bdesc, IDESC_O,
-                     (i > 0 || kk > 0) ? 1u : 0u);
+          mma_f16_ts(tmem + static_cast<uint32_t>(t * D), pa + static_cast<uint32_t>(kk * 8),
+                     bdesc, IDESC_O, (i > 0 || kk > 0) ? 1u : 0u);
         }
         mma_commit(smem_u32(&sh.pv_done[t][b]));
       }
@@ -234,7 +217,7 @@ __global__ void __launch_bounds__(NT == 1 ? 256 : 384, 1)
       const uint32_t ks = kv_smem + s * kv_stage;
 #pragma unroll
       for (int t = 0; t < NT; ++t) {
-        if (j >= nblk[t]) continue;
+        if (j >= nblk_of(t)) continue;
         if (!mbar_wait(smem_u32(&sh.s_free[t][b]), (u & 1u) ^ 1u, abort_flag, err,
                        kErrWaitMma)) {
           ok = false;
@@ -272,7 +255,7 @@ __global__ void __launch_bounds__(NT == 1 ? 256 : 384, 1)
     const int row = q * 32 + lane;     // query row within the tile == TMEM lane
     const int tq0 = q0 + 128 * tile;
     const int qrow = tq0 + row;
-    const int my_nblk = nblk[tile];
+    const int my_nblk = nblk_of(tile);
     const uint32_t lane_addr = static_cast<uint32_t>(q * 32) << 16;
     const uint32_t o_tmem = tmem + static_cast<uint32_t>(tile * D);
     float m_used = -INFINITY;
@@ -361,30 +344,25 @@ __global__ void __launch_bounds__(NT == 1 ? 256 : 384, 1)
         rs8[i & 7] += sv[i];
       }
       l += ((rs8[0] + rs8[1]) + (rs8[2] + rs8[3])) + ((rs8[4] + rs8[5]) + (rs8[6] + rs8[7]));
-      if (j >= 2) {
-        const int pj = j - 2;
-        if (!mbar_wait(smem_u32(&sh.pv_done[tile][pj & 1]), static_cast<uint32_t>(pj >> 1) & 1u,
-                       abort_flag, err, kErrWaitSoftmax)) {
-          ok = false;
-          break;
-        }
-      }
-      uint8_t* pbuf = p_generic + (tile * 2 + b) * p_stride;
+      // P_j -> TMEM over the first BN/2 columns of its own S buffer (S_j
+      // has been read).  The MMA issuer writes S_{j+2} into this buffer only
+      // after issuing PV_j, and tcgen05 MMAs execute in issue order.
+      {
+        uint32_t pk[BN / 2];
 #pragma unroll
-      for (int g = 0; g < BN / 8; ++g) {
-        uint4 v4;
-        if constexpr (FMT == 1) {
-          v4 = make_uint4(pack_bf16(sv[8 * g], sv[8 * g + 1]), pack_bf16(sv[8 * g + 2], sv[8 * g + 3]),
-                          pack_bf16(sv[8 * g + 4], sv[8 * g + 5]),
-                          pack_bf16(sv[8 * g + 6], sv[8 * g + 7]));
+        for (int g = 0; g < BN / 2; ++g)
+          pk[g] = FMT == 1 ? pack_bf16(sv[2 * g], sv[2 * g + 1]) : pack_f16(sv[2 * g], sv[2 * g + 1]);
+        const uint32_t pa = tmem + lane_addr + static_cast<uint32_t>(NT * D + (tile * 2 + b) * BN);
+        if constexpr (BN / 2 >= 32) {
+#pragma unroll
+          for (int c = 0; c < BN / 64; ++c)
+            tmem_st32(pa + static_cast<uint32_t>(c * 32),
+                      *reinterpret_cast<const uint32_t(*)[32]>(pk + c * 32));
         } else {
-          v4 = make_uint4(pack_f16(sv[8 * g], sv[8 * g + 1]), pack_f16(sv[8 * g + 2], sv[8 * g + 3]),
-                          pack_f16(sv[8 * g + 4], sv[8 * g + 5]),
-                          pack_f16(sv[8 * g + 6], sv[8 * g + 7]));
+          tmem_st16(pa, pk);
         }
-        *reinterpret_cast<uint4*>(pbuf + kmajor_swizzled(row, g * 16, SWP)) = v4;
+        tmem_wait_st();
       }
-      fence_proxy_async_smem();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(smem_u32(&sh.p_full[tile][b]));
@@ -452,9 +430,8 @@ static bool encode_bsd(CUtensorMap* map, CUtensorMapDataType dt, const void* ptr
 
 static uint32_t attn_tc_smem(int BN, int D, int stages, int nt) {
   auto al = [](uint32_t x) { return (x + 1023u) & ~1023u; };
-  const uint32_t q = 128u * D * 2, p = 128u * BN * 2, kv = static_cast<uint32_t>(BN) * D * 2;
-  return static_cast<uint32_t>(nt) * (al(q) + 2 * al(p)) +
-         static_cast<uint32_t>(stages) * 2 * al(kv) + 1024u;
+  const uint32_t q = 128u * D * 2, kv = static_cast<uint32_t>(BN) * D * 2;
+  return static_cast<uint32_t>(nt) * al(q) + static_cast<uint32_t>(stages) * 2 * al(kv) + 1024u;
 }
 
 // Plan: aux[0] = dynamic smem bytes, aux[1] = query tiles per CTA (NT).
@@ -478,7 +455,7 @@ gpo_status plan_attention_tc(const gpo_key& k, Plan& p, std::string& log) {
   const uint32_t smem = dyn + static_cast<uint32_t>(sizeof(AttnShared));
   if (smem > kMaxSmemPerCta) {
     log = "shared memory " + std::to_string(smem) + " B (" + std::to_string(nt) +
-          " x (Q + 2 P buffers), " + std::to_string(k.num_stages) +
+          " Q tiles, " + std::to_string(k.num_stages) +
           " K/V stages) exceeds the 232448 B per-CTA limit";
     return GPO_COMPILE_ERROR;
   }
