@@ -359,17 +359,19 @@ def run_reference(args, rank, world):
 
 # ------------------------------------------------------------ extras
 EXTRA_TASKS = [
-    ("vecadd", (1 << 24,), {"BLOCK_SIZE": 4096, "num_warps": 8, "dtype": "float32"}),
+    ("vecadd", (1 << 24,), {"BLOCK_SIZE": 2048, "num_warps": 4, "dtype": "float32"}),
     ("softmax", (16384, 8192), {"BLOCK_N": 8192, "num_warps": 8, "num_stages": 2,
                                 "dtype": "bfloat16"}),
     ("layernorm", (16384, 8192), {"BLOCK_N": 8192, "num_warps": 16, "num_stages": 2,
                                   "dtype": "bfloat16"}),
     ("reduction", (1 << 28,), {"BLOCK_SIZE": 8192, "num_warps": 16, "strategy": "atomic",
                                "dtype": "float32"}),
-    ("fused_gelu", (1 << 26,), {"BLOCK_SIZE": 4096, "num_warps": 8, "strategy": "fused",
+    ("fused_gelu", (1 << 26,), {"BLOCK_SIZE": 4096, "num_warps": 4, "strategy": "fused",
                                 "dtype": "bfloat16"}),
     ("attention_causal", (128, 4096, 128), {"BLOCK_M": 128, "BLOCK_N": 128, "num_warps": 4,
-                                            "num_stages": 3, "dtype": "bfloat16"}),
+                                            "num_stages": 2, "dtype": "bfloat16"}),
+    ("attention", (128, 4096, 128), {"BLOCK_M": 128, "BLOCK_N": 128, "num_warps": 4,
+                                     "num_stages": 2, "dtype": "bfloat16"}),
     ("matmul", (8192, 8192, 8192), {"BLOCK_M": 256, "BLOCK_N": 256, "BLOCK_K": 64,
                                     "GROUP_M": 16, "num_warps": 4, "num_stages": 3,
                                     "dtype": "bfloat16"}),

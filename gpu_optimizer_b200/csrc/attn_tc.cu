@@ -5,28 +5,35 @@
 // inputs with BLOCK_M = 128.  One CTA per (128-row query tile, batch*head);
 // causal grids visit the longest query tiles first.
 //
-// Warp roles (8 warps):
-//   warp 0  TMA producer: Q once, then K_j and V_j into a num_stages ring.
-//   warp 1  MMA issuer:   S_j = Q K_j^T into TMEM buffer j%2, then
-//                         O += P_{j-1} V_{j-1} (one block behind, so the
-//                         softmax of block j overlaps S_{j+1} and PV_{j-1}).
+// Warp roles (num_warps 4 -> 8 warps):
+//   warp 0  TMA producer of Q (once) and of the K ring (num_stages slots).
+//   warp 3  TMA producer of the V ring (num_stages slots).  K slot j is
+//           released when S_j's MMAs complete, V slot j when PV_j's do, so
+//           neither ring waits on the other.
+//   warp 1  MMA issuer:   S_j = Q K_j^T into TMEM buffer j % NB, then
+//                         O += P_i V_i for i = j - (NB - 1).  With NB = 3
+//                         S/P buffers the S MMAs run two blocks ahead of the
+//                         PV MMAs, so the softmax of block j overlaps the
+//                         MMAs of S_{j+1}, S_{j+2} and PV_{j-1}.
 //   warp 2  TMEM owner.
 //   warps 4-7 softmax / correction / epilogue: thread r owns query row r
 //           (TMEM lane r).  It reads S_j from TMEM, applies scale, padding
 //           and causal masks, keeps the running max in the log2 domain,
 //           writes P_j = exp2(s - m) as 16-bit pairs back into TMEM over its
 //           own S buffer (the A operand of the PV MMA, read from TMEM) and
-//           accumulates the fp32 row sum.  The running max used for P is only moved (and O in
-//           TMEM rescaled) when a block's max exceeds it by more than 8
-//           (a factor of 256); until then P <= 256, which 16-bit P and the
-//           fp32 accumulator represent exactly as well as P <= 1.
+//           accumulates the fp32 row sum.  Scale/shift FMAs and row-sum adds
+//           run as packed fp32x2 operations and the row max as three-input
+//           max, so the exp2 on the MUFU unit dominates the instruction mix.
+//           The running max used for P is only moved (and O in TMEM
+//           rescaled) when a block's max exceeds it by more than 8 (a factor
+//           of 256); until then P <= 256, which 16-bit P and the fp32
+//           accumulator represent exactly as well as P <= 1.
 // num_warps 8 doubles the CTA: two softmax warpgroups (warps 4-7 and 8-11),
 // each owning its own 128-row query tile, share every K/V tile; the MMA
-// issuer interleaves S_A(j), S_B(j), PV_A(j-1), PV_B(j-1), so one group's
-// softmax overlaps the other's MMAs and each SM sub-partition runs two
-// softmax warps.
-// TMEM columns per tile t of NT: O_t [t*D, t*D+D), S_t buffers
-// [NT*D + (2t+b)*BN, +BN) for b in {0, 1}.
+// issuer interleaves both tiles' S and PV MMAs.
+// TMEM columns per tile t of NT: O_t [t*D, t*D+D), S/P buffers
+// [NT*D + (NB*t+b)*BN, +BN) for b < NB; NB = 3 when NT*(D + 3*BN) <= 512,
+// else 2.
 #include <algorithm>
 
 #include "gpo_common.cuh"
@@ -38,16 +45,22 @@ constexpr int kAttnMaxStages = 4;
 constexpr float kRescaleThreshold = 8.0f;
 
 constexpr int kAttnMaxTiles = 2;  // query tiles (softmax warpgroups) per CTA
+constexpr int kAttnMaxSBufs = 3;  // S/P buffers per query tile
+
+// S/P buffers per query tile: three when TMEM has room, else two.
+__host__ __device__ constexpr int attn_sbufs(int nt, int d, int bn) {
+  return nt * (d + 3 * bn) <= 512 ? 3 : 2;
+}
 
 struct AttnShared {
   uint64_t q_full;
   uint64_t k_full[kAttnMaxStages];
+  uint64_t k_empty[kAttnMaxStages];
   uint64_t v_full[kAttnMaxStages];
-  uint64_t kv_empty[kAttnMaxStages];
-  uint64_t s_full[kAttnMaxTiles][2];
-  uint64_t s_free[kAttnMaxTiles][2];
-  uint64_t p_full[kAttnMaxTiles][2];
-  uint64_t pv_done[kAttnMaxTiles][2];
+  uint64_t v_empty[kAttnMaxStages];
+  uint64_t s_full[kAttnMaxTiles][kAttnMaxSBufs];
+  uint64_t p_full[kAttnMaxTiles][kAttnMaxSBufs];
+  uint64_t pv_done[kAttnMaxTiles][kAttnMaxSBufs];
   uint64_t drain;
   uint32_t tmem_base;
   int abort;
@@ -55,6 +68,12 @@ struct AttnShared {
 
 __host__ __device__ constexpr int attn_tmem_alloc(int cols) {
   return cols <= 32 ? 32 : cols <= 64 ? 64 : cols <= 128 ? 128 : cols <= 256 ? 256 : 512;
+}
+
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
 }
 
 template <typename T, int FMT, int BN, int D, bool CAUSAL, int NT>
@@ -67,18 +86,21 @@ __global__ void __launch_bounds__(NT == 1 ? 256 : 384, 1)
   constexpr int SWQ = (D * ES) < 128 ? (D * ES) : 128;  // swizzle of Q/K/V rows
   constexpr uint32_t Q_BYTES = 128u * D * ES;
   constexpr uint32_t KV_BYTES = static_cast<uint32_t>(BN) * D * ES;
-  constexpr int COLS = NT * D + NT * 2 * BN;
+  constexpr uint32_t KV_SLOT = (KV_BYTES + 1023u) & ~1023u;
+  constexpr int NB = attn_sbufs(NT, D, BN);
+  constexpr int LAG = NB - 1;  // S MMAs run LAG blocks ahead of PV MMAs
+  constexpr int COLS = NT * D + NT * NB * BN;
   constexpr int ALLOC = attn_tmem_alloc(COLS);
   constexpr uint32_t IDESC_S = make_idesc(FMT, 128, BN, false, false);
   constexpr uint32_t IDESC_O = make_idesc(FMT, 128, D, false, true);
+  static_assert(COLS <= 512, "TMEM holds 512 columns");
 
   __shared__ AttnShared sh;
   extern __shared__ uint8_t dyn_smem[];
   const uint32_t base = (smem_u32(dyn_smem) + 1023u) & ~1023u;
-  const uint32_t q_smem = base;                             // NT tiles
-  const uint32_t kv_smem = q_smem + NT * Q_BYTES;
-  const uint32_t kv_stage = 2 * ((KV_BYTES + 1023u) & ~1023u);
-  const uint32_t v_off = (KV_BYTES + 1023u) & ~1023u;
+  const uint32_t q_smem = base;  // NT tiles
+  const uint32_t k_smem = q_smem + NT * Q_BYTES;
+  const uint32_t v_smem = k_smem + static_cast<uint32_t>(stages) * KV_SLOT;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   constexpr int CTA_ROWS = 128 * NT;
@@ -100,13 +122,13 @@ __global__ void __launch_bounds__(NT == 1 ? 256 : 384, 1)
     mbar_init(smem_u32(&sh.q_full), 1);
     for (int s = 0; s < stages; ++s) {
       mbar_init(smem_u32(&sh.k_full[s]), 1);
+      mbar_init(smem_u32(&sh.k_empty[s]), 1);
       mbar_init(smem_u32(&sh.v_full[s]), 1);
-      mbar_init(smem_u32(&sh.kv_empty[s]), 1);
+      mbar_init(smem_u32(&sh.v_empty[s]), 1);
     }
     for (int t = 0; t < NT; ++t)
-      for (int b = 0; b < 2; ++b) {
+      for (int b = 0; b < NB; ++b) {
         mbar_init(smem_u32(&sh.s_full[t][b]), 1);
-        mbar_init(smem_u32(&sh.s_free[t][b]), 4);
         mbar_init(smem_u32(&sh.p_full[t][b]), 4);
         mbar_init(smem_u32(&sh.pv_done[t][b]), 1);
       }
@@ -127,66 +149,65 @@ __global__ void __launch_bounds__(NT == 1 ? 256 : 384, 1)
   const uint32_t tmem = sh.tmem_base;
   volatile int* abort_flag = &sh.abort;
 
-  if (warp == 0 && lane == 0) {
-    // ------------------------------------------------------------ producer
+  if ((warp == 0 || warp == 3) && lane == 0) {
+    // ----------------------------------------------- producers (K: 0, V: 3)
+    const bool is_k = warp == 0;
+    const CUtensorMap* map = is_k ? &tma_k : &tma_v;
+    const uint32_t ring = is_k ? k_smem : v_smem;
+    uint64_t* full = is_k ? sh.k_full : sh.v_full;
+    uint64_t* empty = is_k ? sh.k_empty : sh.v_empty;
+    const uint32_t site = kErrWaitProducer;
     bool ok = true;
     int issued = 0;
-    mbar_arrive_expect_tx(smem_u32(&sh.q_full), NT * Q_BYTES);
+    if (is_k) {
+      mbar_arrive_expect_tx(smem_u32(&sh.q_full), NT * Q_BYTES);
 #pragma unroll
-    for (int t = 0; t < NT; ++t)
+      for (int t = 0; t < NT; ++t)
 #pragma unroll
-      for (int a = 0; a < (D * ES) / SWQ; ++a)
-        tma_load_3d(q_smem + t * Q_BYTES + a * 128 * SWQ, &tma_q, smem_u32(&sh.q_full),
-                    a * (SWQ / ES), q0 + 128 * t, bh);
+        for (int a = 0; a < (D * ES) / SWQ; ++a)
+          tma_load_3d(q_smem + t * Q_BYTES + a * 128 * SWQ, &tma_q, smem_u32(&sh.q_full),
+                      a * (SWQ / ES), q0 + 128 * t, bh);
+    }
     for (int j = 0; j < nblk_max; ++j) {
       const int s = j % stages;
       const uint32_t r = static_cast<uint32_t>(j / stages);
-      if (!mbar_wait(smem_u32(&sh.kv_empty[s]), (r & 1u) ^ 1u, abort_flag, err,
-                     kErrWaitProducer)) {
+      if (!mbar_wait(smem_u32(&empty[s]), (r & 1u) ^ 1u, abort_flag, err, site)) {
         ok = false;
         break;
       }
-      const uint32_t ks = kv_smem + s * kv_stage;
-      const uint32_t kf = smem_u32(&sh.k_full[s]), vf = smem_u32(&sh.v_full[s]);
-      mbar_arrive_expect_tx(kf, KV_BYTES);
+      const uint32_t fb = smem_u32(&full[s]);
+      const uint32_t dst = ring + static_cast<uint32_t>(s) * KV_SLOT;
+      mbar_arrive_expect_tx(fb, KV_BYTES);
 #pragma unroll
       for (int a = 0; a < (D * ES) / SWQ; ++a)
-        tma_load_3d(ks + a * BN * SWQ, &tma_k, kf, a * (SWQ / ES), j * BN, bh);
-      mbar_arrive_expect_tx(vf, KV_BYTES);
-#pragma unroll
-      for (int a = 0; a < (D * ES) / SWQ; ++a)
-        tma_load_3d(ks + v_off + a * BN * SWQ, &tma_v, vf, a * (SWQ / ES), j * BN, bh);
+        tma_load_3d(dst + a * BN * SWQ, map, fb, a * (SWQ / ES), j * BN, bh);
       issued = j + 1;
     }
     if (!ok) {
-      mbar_wait_drain(smem_u32(&sh.q_full), 0, err);
-      for (int j = max(0, issued - stages); j < issued; ++j) {
-        mbar_wait_drain(smem_u32(&sh.k_full[j % stages]), static_cast<uint32_t>(j / stages) & 1u,
-                        err);
-        mbar_wait_drain(smem_u32(&sh.v_full[j % stages]), static_cast<uint32_t>(j / stages) & 1u,
-                        err);
-      }
+      if (is_k) mbar_wait_drain(smem_u32(&sh.q_full), 0, err);
+      for (int j = max(0, issued - stages); j < issued; ++j)
+        mbar_wait_drain(smem_u32(&full[j % stages]), static_cast<uint32_t>(j / stages) & 1u, err);
     }
   } else if (warp == 1 && lane == 0) {
     // ---------------------------------------------------------- MMA issuer
     bool ok = mbar_wait(smem_u32(&sh.q_full), 0, abort_flag, err, kErrWaitMma);
     // O_t += P_t(i) V(i) for every tile that still needs block i, then
-    // release the K/V stage of block i.
+    // release V slot i.
     auto pv_round = [&](int i) -> bool {
       const int s = i % stages;
       const uint32_t r = static_cast<uint32_t>(i / stages);
-      const int b = i & 1;
-      const uint32_t u = static_cast<uint32_t>(i >> 1);
+      const int b = i % NB;
+      const uint32_t u = static_cast<uint32_t>(i / NB);
       if (!mbar_wait(smem_u32(&sh.v_full[s]), r & 1u, abort_flag, err, kErrWaitMma)) return false;
-      const uint32_t vs = kv_smem + s * kv_stage + v_off;
+      const uint32_t vs = v_smem + static_cast<uint32_t>(s) * KV_SLOT;
 #pragma unroll
       for (int t = 0; t < NT; ++t) {
         if (i >= nblk_of(t)) continue;
         if (!mbar_wait(smem_u32(&sh.p_full[t][b]), u & 1u, abort_flag, err, kErrWaitMma))
           return false;
         tc_fence_after();
-        // P_t(i) sits in the first BN/2 columns of S buffer b (16-bit pairs)
-        const uint32_t pa = tmem + static_cast<uint32_t>(NT * D + (t * 2 + b) * BN);
+        // P_t(i) sits in the first BN/2 columns of S/P buffer b (16-bit pairs)
+        const uint32_t pa = tmem + static_cast<uint32_t>(NT * D + (t * NB + b) * BN);
 #pragma unroll
         for (int kk = 0; kk < BN / 16; ++kk) {
           const uint64_t bdesc = make_smem_desc(vs + kk * 16 * SWQ, BN * SWQ, 8 * SWQ, SWQ);
@@ -195,36 +216,25 @@ __global__ void __launch_bounds__(NT == 1 ? 256 : 384, 1)
         }
         mma_commit(smem_u32(&sh.pv_done[t][b]));
       }
-      mma_commit(smem_u32(&sh.kv_empty[s]));
+      mma_commit(smem_u32(&sh.v_empty[s]));
       return true;
     };
-    // With a single K/V stage, K_j can only land after block j-1's PV frees
-    // the stage, so that PV round is issued before S_j instead of after it.
-    const bool pv_first = stages == 1;
     for (int j = 0; j < nblk_max && ok; ++j) {
       const int s = j % stages;
       const uint32_t r = static_cast<uint32_t>(j / stages);
-      const int b = j & 1;
-      const uint32_t u = static_cast<uint32_t>(j >> 1);
-      if (pv_first && j > 0 && !pv_round(j - 1)) {
-        ok = false;
-        break;
-      }
+      const int b = j % NB;
       if (!mbar_wait(smem_u32(&sh.k_full[s]), r & 1u, abort_flag, err, kErrWaitMma)) {
         ok = false;
         break;
       }
-      const uint32_t ks = kv_smem + s * kv_stage;
+      tc_fence_after();
+      const uint32_t ks = k_smem + static_cast<uint32_t>(s) * KV_SLOT;
 #pragma unroll
       for (int t = 0; t < NT; ++t) {
         if (j >= nblk_of(t)) continue;
-        if (!mbar_wait(smem_u32(&sh.s_free[t][b]), (u & 1u) ^ 1u, abort_flag, err,
-                       kErrWaitMma)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        const uint32_t s_tmem = tmem + static_cast<uint32_t>(NT * D + (t * 2 + b) * BN);
+        // Buffer b last held P_t(j - NB), whose PV MMA this thread issued
+        // earlier; tcgen05 MMAs of one thread execute in issue order.
+        const uint32_t s_tmem = tmem + static_cast<uint32_t>(NT * D + (t * NB + b) * BN);
         const uint32_t qs = q_smem + t * Q_BYTES;
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
@@ -237,13 +247,13 @@ __global__ void __launch_bounds__(NT == 1 ? 256 : 384, 1)
         }
         mma_commit(smem_u32(&sh.s_full[t][b]));
       }
-      if (!ok) break;
-      if (!pv_first && j > 0 && !pv_round(j - 1)) {
+      mma_commit(smem_u32(&sh.k_empty[s]));
+      if (j >= LAG && !pv_round(j - LAG)) {
         ok = false;
         break;
       }
     }
-    if (ok && nblk_max > 0) ok = pv_round(nblk_max - 1);
+    for (int i = max(0, nblk_max - LAG); i < nblk_max && ok; ++i) ok = pv_round(i);
     if (!ok) {
       mma_commit(smem_u32(&sh.drain));
       mbar_wait_drain(smem_u32(&sh.drain), 0, err);
@@ -258,12 +268,14 @@ __global__ void __launch_bounds__(NT == 1 ? 256 : 384, 1)
     const int my_nblk = nblk_of(tile);
     const uint32_t lane_addr = static_cast<uint32_t>(q * 32) << 16;
     const uint32_t o_tmem = tmem + static_cast<uint32_t>(tile * D);
+    const float2 scale2 = make_float2(scale_log2, scale_log2);
     float m_used = -INFINITY;
     float l = 0.f;
     bool ok = true;
     for (int j = 0; j < my_nblk; ++j) {
-      const int b = j & 1;
-      const uint32_t u = static_cast<uint32_t>(j >> 1);
+      const int b = j % NB;
+      const uint32_t u = static_cast<uint32_t>(j / NB);
+      const uint32_t sp = tmem + lane_addr + static_cast<uint32_t>(NT * D + (tile * NB + b) * BN);
       if (!mbar_wait(smem_u32(&sh.s_full[tile][b]), u & 1u, abort_flag, err, kErrWaitSoftmax)) {
         ok = false;
         break;
@@ -275,15 +287,12 @@ __global__ void __launch_bounds__(NT == 1 ? 256 : 384, 1)
         uint32_t r[BN];
 #pragma unroll
         for (int c = 0; c < BN / 32; ++c)
-          tmem_ld32(tmem + lane_addr + static_cast<uint32_t>(NT * D + (tile * 2 + b) * BN + c * 32),
+          tmem_ld32(sp + static_cast<uint32_t>(c * 32),
                     *reinterpret_cast<uint32_t(*)[32]>(r + c * 32));
         tmem_wait_ld();
 #pragma unroll
         for (int i = 0; i < BN; ++i) sv[i] = __uint_as_float(r[i]);
       }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(smem_u32(&sh.s_free[tile][b]));
 
       // Mask padding / future keys only where the block needs it (block-
       // uniform test on the tile's first row); work on raw scores, with the
@@ -297,14 +306,11 @@ __global__ void __launch_bounds__(NT == 1 ? 256 : 384, 1)
           if (key >= S || (CAUSAL && key > qrow)) sv[i] = -INFINITY;
         }
       }
-      float mx8[8];
+      // row max: four independent three-input max chains
+      float mx[4] = {sv[0], sv[1], sv[2], sv[3]};
 #pragma unroll
-      for (int t = 0; t < 8; ++t) mx8[t] = sv[t];
-#pragma unroll
-      for (int i = 8; i < BN; ++i) mx8[i & 7] = fmaxf(mx8[i & 7], sv[i]);
-      const float mb = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
-                             fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7]))) *
-                       scale_log2;
+      for (int i = 4; i + 1 < BN; i += 2) mx[(i >> 1) & 3] = fmax3(mx[(i >> 1) & 3], sv[i], sv[i + 1]);
+      const float mb = fmaxf(fmax3(mx[0], mx[1], mx[2]), mx[3]) * scale_log2;
       if (j == 0) {
         m_used = mb;
       } else {
@@ -314,8 +320,8 @@ __global__ void __launch_bounds__(NT == 1 ? 256 : 384, 1)
           const float alpha = ex2_approx(m_used - m_new);
           // O holds PV_0..PV_{j-1}; wait for PV_{j-1} before rescaling it
           const int pj = j - 1;
-          if (!mbar_wait(smem_u32(&sh.pv_done[tile][pj & 1]), static_cast<uint32_t>(pj >> 1) & 1u,
-                         abort_flag, err, kErrWaitSoftmax)) {
+          if (!mbar_wait(smem_u32(&sh.pv_done[tile][pj % NB]),
+                         static_cast<uint32_t>(pj / NB) & 1u, abort_flag, err, kErrWaitSoftmax)) {
             ok = false;
             break;
           }
@@ -335,34 +341,35 @@ __global__ void __launch_bounds__(NT == 1 ? 256 : 384, 1)
           m_used = m_new;
         }
       }
-      // P_j = exp2(s * scale - m_used); 8 independent partial sums
+      // P_j = exp2(s * scale - m_used) with packed fp32x2 FMAs, row sum in
+      // four packed partial sums
       const float neg_m = (m_used == -INFINITY) ? 0.f : -m_used;
-      float rs8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+      const float2 shift2 = make_float2(neg_m, neg_m);
+      float2 rs[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f),
+                      make_float2(0.f, 0.f)};
+      uint32_t pk[BN / 2];
 #pragma unroll
-      for (int i = 0; i < BN; ++i) {
-        sv[i] = ex2_approx(fmaf(sv[i], scale_log2, neg_m));  // -inf -> 0
-        rs8[i & 7] += sv[i];
+      for (int g = 0; g < BN / 2; ++g) {
+        const float2 x = __ffma2_rn(make_float2(sv[2 * g], sv[2 * g + 1]), scale2, shift2);
+        const float2 p = make_float2(ex2_approx(x.x), ex2_approx(x.y));  // -inf -> 0
+        rs[g & 3] = __fadd2_rn(rs[g & 3], p);
+        pk[g] = FMT == 1 ? pack_bf16(p.x, p.y) : pack_f16(p.x, p.y);
       }
-      l += ((rs8[0] + rs8[1]) + (rs8[2] + rs8[3])) + ((rs8[4] + rs8[5]) + (rs8[6] + rs8[7]));
+      const float2 rs01 = __fadd2_rn(rs[0], rs[1]), rs23 = __fadd2_rn(rs[2], rs[3]);
+      const float2 rsum = __fadd2_rn(rs01, rs23);
+      l += rsum.x + rsum.y;
       // P_j -> TMEM over the first BN/2 columns of its own S buffer (S_j
-      // has been read).  The MMA issuer writes S_{j+2} into this buffer only
-      // after issuing PV_j, and tcgen05 MMAs execute in issue order.
-      {
-        uint32_t pk[BN / 2];
+      // has been read).  The MMA issuer writes S_{j+NB} into this buffer
+      // only after issuing PV_j, and tcgen05 MMAs execute in issue order.
+      if constexpr (BN / 2 >= 32) {
 #pragma unroll
-        for (int g = 0; g < BN / 2; ++g)
-          pk[g] = FMT == 1 ? pack_bf16(sv[2 * g], sv[2 * g + 1]) : pack_f16(sv[2 * g], sv[2 * g + 1]);
-        const uint32_t pa = tmem + lane_addr + static_cast<uint32_t>(NT * D + (tile * 2 + b) * BN);
-        if constexpr (BN / 2 >= 32) {
-#pragma unroll
-          for (int c = 0; c < BN / 64; ++c)
-            tmem_st32(pa + static_cast<uint32_t>(c * 32),
-                      *reinterpret_cast<const uint32_t(*)[32]>(pk + c * 32));
-        } else {
-          tmem_st16(pa, pk);
-        }
-        tmem_wait_st();
+        for (int c = 0; c < BN / 64; ++c)
+          tmem_st32(sp + static_cast<uint32_t>(c * 32),
+                    *reinterpret_cast<const uint32_t(*)[32]>(pk + c * 32));
+      } else {
+        tmem_st16(sp, pk);
       }
+      tmem_wait_st();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(smem_u32(&sh.p_full[tile][b]));
@@ -370,7 +377,7 @@ __global__ void __launch_bounds__(NT == 1 ? 256 : 384, 1)
     // ------------------------------------------------------------ epilogue
     if (ok && my_nblk > 0) {
       const int pj = my_nblk - 1;
-      ok = mbar_wait(smem_u32(&sh.pv_done[tile][pj & 1]), static_cast<uint32_t>(pj >> 1) & 1u,
+      ok = mbar_wait(smem_u32(&sh.pv_done[tile][pj % NB]), static_cast<uint32_t>(pj / NB) & 1u,
                      abort_flag, err, kErrWaitSoftmax);
     }
     if (ok) {
@@ -444,13 +451,14 @@ gpo_status plan_attention_tc(const gpo_key& k, Plan& p, std::string& log) {
     log = "num_stages must be in [1, 4]";
     return GPO_BAD_CONFIG;
   }
-  const int cols_needed = nt * D + nt * 2 * BN;
-  if (cols_needed > static_cast<int>(kTmemCols)) {
-    log = "TMEM needs " + std::to_string(cols_needed) + " columns (" + std::to_string(nt) +
+  const int min_cols = nt * (D + 2 * BN);
+  if (min_cols > static_cast<int>(kTmemCols)) {
+    log = "TMEM needs " + std::to_string(min_cols) + " columns (" + std::to_string(nt) +
           " query tiles x (O " + std::to_string(D) + " + 2 S buffers x " + std::to_string(BN) +
           ")) > 512";
     return GPO_COMPILE_ERROR;
   }
+  const int cols_needed = nt * (D + attn_sbufs(nt, D, BN) * BN);
   const uint32_t dyn = attn_tc_smem(BN, D, k.num_stages, nt);
   const uint32_t smem = dyn + static_cast<uint32_t>(sizeof(AttnShared));
   if (smem > kMaxSmemPerCta) {
@@ -469,9 +477,9 @@ gpo_status plan_attention_tc(const gpo_key& k, Plan& p, std::string& log) {
   p.res.grid_y = static_cast<uint32_t>(k.shape[0]);
   p.res.grid_z = 1;
   p.res.launches_per_call = 1;
-  snprintf(p.res.kernel, sizeof(p.res.kernel), "attn_tc_kernel<%s,BN=%d,D=%d,%s,tiles=%d>",
+  snprintf(p.res.kernel, sizeof(p.res.kernel), "attn_tc_kernel<%s,BN=%d,D=%d,%s,tiles=%d,sbufs=%d>",
            k.dtype == GPO_BFLOAT16 ? "bf16" : "f16", BN, D,
-           k.task == GPO_TASK_ATTENTION_CAUSAL ? "causal" : "full", nt);
+           k.task == GPO_TASK_ATTENTION_CAUSAL ? "causal" : "full", nt, attn_sbufs(nt, D, BN));
   return GPO_OK;
 }
 
@@ -500,7 +508,7 @@ static gpo_status run_attn_tc_nt(const gpo_key& k, const Plan& p, const gpo_args
 template <typename T, int FMT, int BN, int D, bool CAUSAL>
 static gpo_status run_attn_tc(const gpo_key& k, const Plan& p, const gpo_args& a,
                               const LaunchCtx& c, CUtensorMapDataType dt) {
-  if constexpr (2 * D + 4 * BN <= 512) {
+  if constexpr (2 * (D + 2 * BN) <= 512) {
     if (p.aux[1] == 2) return run_attn_tc_nt<T, FMT, BN, D, CAUSAL, 2>(k, p, a, c, dt);
   }
   if (p.aux[1] != 1) return GPO_INTERNAL;

@@ -74,11 +74,11 @@ def test_attention_plans():
     base = {"BLOCK_M": 128, "BLOCK_N": 128, "num_warps": 4, "num_stages": 2,
             "dtype": "bfloat16"}
     r = compile_module("attention_causal", (128, 4096, 128), base).resources()
-    assert r["kernel"] == "attn_tc_kernel<bf16,BN=128,D=128,causal,tiles=1>"
+    assert r["kernel"] == "attn_tc_kernel<bf16,BN=128,D=128,causal,tiles=1,sbufs=3>"
     assert r["tmem_cols"] == 512 and r["grid"] == [32, 128, 1]
     r2 = compile_module("attention_causal", (128, 4096, 128),
                         {**base, "BLOCK_N": 64, "num_warps": 8}).resources()
-    assert r2["kernel"].endswith("tiles=2>") and r2["threads_per_cta"] == 384
+    assert r2["kernel"].endswith("tiles=2,sbufs=2>") and r2["threads_per_cta"] == 384
     assert r2["grid"] == [16, 128, 1] and r2["tmem_cols"] == 512
     with pytest.raises(KernelBuildError) as ei:  # 2 x (O 128 + 2 x S 128) columns
         compile_module("attention_causal", (128, 4096, 128), {**base, "num_warps": 8})
