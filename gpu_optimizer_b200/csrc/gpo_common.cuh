@@ -85,6 +85,13 @@ __device__ __forceinline__ void mbar_arrive(uint32_t bar) {
                : "memory");
 }
 
+// Arrive on an mbarrier of any CTA of the cluster (a shared::cluster address
+// from mapa_shared), releasing this thread's prior writes at cluster scope.
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr)
+               : "memory");
+}
+
 __device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t bar, uint32_t bytes) {
   asm volatile(
       "{\n\t.reg .b64 st;\n\tmbarrier.arrive.expect_tx.shared::cta.b64 st, [%0], %1;\n\t}" ::"r"(
@@ -105,16 +112,58 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   return ok != 0;
 }
 
+// try_wait with cluster-scope acquire: pairs with mbar_arrive_cluster from
+// the peer CTA.
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
 // Bounded wait for the phase of `bar` with the given parity to complete.
 // Returns false (after recording `site` in *err and raising *abort) when the
 // time limit passes or another role already aborted the CTA.
+template <bool CLUSTER = false>
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort,
                                           unsigned int* err, uint32_t site) {
-  if (mbar_try_wait(bar, parity)) return true;
+  auto probe = [&] {
+    return CLUSTER ? mbar_try_wait_cluster(bar, parity) : mbar_try_wait(bar, parity);
+  };
+  if (probe()) return true;
   const unsigned long long t0 = globaltimer_ns();
   for (uint32_t it = 1;; ++it) {
-    if (mbar_try_wait(bar, parity)) return true;
+    if (probe()) return true;
     if ((it & 255u) == 0) {
+      if (*abort) return false;
+      if (globaltimer_ns() - t0 > kWaitLimitNs) {
+        atomicOr(err, site);
+        *abort = 1;
+        return false;
+      }
+    }
+  }
+}
+
+// Bounded wait for roles that idle for a whole main loop (epilogue warps
+// waiting for an accumulator): polls with a growing __nanosleep back-off so
+// that the waiting warps leave issue slots and the shared-memory barrier
+// unit to the producer and MMA threads.
+__device__ __forceinline__ bool mbar_wait_idle(uint32_t bar, uint32_t parity, volatile int* abort,
+                                               unsigned int* err, uint32_t site) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const unsigned long long t0 = globaltimer_ns();
+  unsigned ns = 32;
+  for (uint32_t it = 1;; ++it) {
+    __nanosleep(ns);
+    if (ns < 512) ns <<= 1;
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((it & 15u) == 0) {
       if (*abort) return false;
       if (globaltimer_ns() - t0 > kWaitLimitNs) {
         atomicOr(err, site);

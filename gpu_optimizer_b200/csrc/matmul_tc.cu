@@ -50,6 +50,11 @@ struct TcShared {
   int abort;
 };
 
+// TMEM allocation (power of two >= 32 columns) for `cols` accumulator columns.
+__host__ __device__ constexpr int tc2_tmem_alloc(int cols) {
+  return cols <= 32 ? 32 : cols <= 64 ? 64 : cols <= 128 ? 128 : cols <= 256 ? 256 : 512;
+}
+
 __device__ __forceinline__ void tile_coords(int tile, int num_pid_m, int num_pid_n, int group_m,
                                             int& pm, int& pn) {
   const int in_group = group_m * num_pid_n;
@@ -58,6 +63,55 @@ __device__ __forceinline__ void tile_coords(int tile, int num_pid_m, int num_pid
   const int gsize = min(num_pid_m - first_m, group_m);
   pm = first_m + (tile % gsize);
   pn = (tile % in_group) / gsize;
+}
+
+// Issue the MMAs of one K block: KS steps of 32 bytes of K (KS =
+// BLOCK_K * es / 32, so the A swizzle width min(KS * 32, 128) is known at
+// compile time too).  a0 / b0 are the descriptors of this ring slot at K
+// step 0; every other descriptor is a compile-time offset from them, which
+// keeps the issuing thread's cost at a few integer ops per MMA -- with
+// runtime offset arithmetic the single issuing thread, not the tensor pipe,
+// bounded the main loop.  AROWS: A rows per swizzle atom column (the CTA's
+// A tile height); HALVES M=128 MMAs per step for 1-CTA BLOCK_M 256.
+template <int KS, int ES, int AROWS, int SWB, int HALVES, int BN, int FMT, bool PAIR>
+__device__ __forceinline__ void issue_kblock(uint32_t d_tmem, uint64_t a0, uint64_t b0,
+                                             uint32_t idesc, bool first) {
+  constexpr int SWA = KS * 32 < 128 ? KS * 32 : 128;
+#pragma unroll
+  for (int kk = 0; kk < KS; ++kk) {
+    const uint32_t kbyte = static_cast<uint32_t>(kk) * 32u;
+    const uint32_t a_off = (kbyte / SWA) * (AROWS * SWA) + (kbyte % SWA);
+    const uint64_t bdesc = b0 + ((static_cast<uint32_t>(kk) * (32 / ES) * SWB) >> 4);
+    const uint32_t acc = (!first || kk > 0) ? 1u : 0u;
+#pragma unroll
+    for (int h = 0; h < HALVES; ++h) {
+      const uint64_t adesc = a0 + ((a_off + h * 128 * SWA) >> 4);
+      if constexpr (PAIR) {
+        if constexpr (FMT == 2)
+          mma_tf32_ss_pair(d_tmem + h * BN, adesc, bdesc, idesc, acc);
+        else
+          mma_f16_ss_pair(d_tmem + h * BN, adesc, bdesc, idesc, acc);
+      } else {
+        if constexpr (FMT == 2)
+          mma_tf32_ss(d_tmem + h * BN, adesc, bdesc, idesc, acc);
+        else
+          mma_f16_ss(d_tmem + h * BN, adesc, bdesc, idesc, acc);
+      }
+    }
+  }
+}
+
+template <int ES, int AROWS, int SWB, int HALVES, int BN, int FMT, bool PAIR>
+__device__ __forceinline__ void issue_kblock_any(int ksteps, uint32_t d_tmem, uint64_t a0,
+                                                 uint64_t b0, uint32_t idesc, bool first) {
+  switch (ksteps) {
+    case 1: issue_kblock<1, ES, AROWS, SWB, HALVES, BN, FMT, PAIR>(d_tmem, a0, b0, idesc, first); break;
+    case 2: issue_kblock<2, ES, AROWS, SWB, HALVES, BN, FMT, PAIR>(d_tmem, a0, b0, idesc, first); break;
+    case 4: issue_kblock<4, ES, AROWS, SWB, HALVES, BN, FMT, PAIR>(d_tmem, a0, b0, idesc, first); break;
+    case 8: issue_kblock<8, ES, AROWS, SWB, HALVES, BN, FMT, PAIR>(d_tmem, a0, b0, idesc, first); break;
+    case 16: issue_kblock<16, ES, AROWS, SWB, HALVES, BN, FMT, PAIR>(d_tmem, a0, b0, idesc, first); break;
+    default: issue_kblock<32, ES, AROWS, SWB, HALVES, BN, FMT, PAIR>(d_tmem, a0, b0, idesc, first); break;
+  }
 }
 
 template <typename T, int FMT, int BM, int BN, bool PERSISTENT>
@@ -121,16 +175,14 @@ __global__ void __launch_bounds__(PERSISTENT ? 256 : 128, 1)
 
   // ------------------------------------------------------------ producer
   if (warp == 0 && lane == 0) {
-    int it = 0;
+    int it = 0, s = 0;  // K blocks issued; ring slot and phase of the next one
+    uint32_t ph = 0;
     bool ok = true;
     for (int tile = blockIdx.x; tile < num_tiles && ok; tile += tile_step) {
       int pm, pn;
       tile_coords(tile, num_pid_m, num_pid_n, group_m, pm, pn);
       for (int kb = 0; kb < num_kb; ++kb, ++it) {
-        const int s = it % stages;
-        const uint32_t r = static_cast<uint32_t>(it / stages);
-        if (!mbar_wait(smem_u32(&sh.empty[s]), (r & 1u) ^ 1u, abort_flag, err,
-                       kErrWaitProducer)) {
+        if (!mbar_wait(smem_u32(&sh.empty[s]), ph ^ 1u, abort_flag, err, kErrWaitProducer)) {
           ok = false;
           break;
         }
@@ -144,6 +196,10 @@ __global__ void __launch_bounds__(PERSISTENT ? 256 : 128, 1)
 #pragma unroll
         for (int c = 0; c < (BN * ES) / SWB; ++c)
           tma_load_2d(sb + c * BK * SWB, &tma_b, full, pn * BN + c * (SWB / ES), kb * BK);
+        if (++s == stages) {
+          s = 0;
+          ph ^= 1u;
+        }
       }
     }
     if (!ok) {
@@ -155,8 +211,21 @@ __global__ void __launch_bounds__(PERSISTENT ? 256 : 128, 1)
   }
   // ---------------------------------------------------------- MMA issuer
   else if (warp == 1 && lane == 0) {
-    int it = 0, tcount = 0;
+    int tcount = 0, s = 0;  // ring slot and phase of the next K block
+    uint32_t ph = 0;
     bool ok = true;
+    // Descriptors of slot 0 at K step 0.  A slot or K step only moves the
+    // start-address field (16-byte units; shared addresses stay below
+    // 2^18 bytes, so adding to the 14-bit field never carries), which keeps
+    // the per-MMA issue cost to a few integer adds.
+    const uint64_t adesc0 = make_smem_desc(smem_base, 16, 8 * swa, swa);
+    // MN-major B.  16-bit: 128/64/32-byte swizzle atoms of 8 K rows.  tf32:
+    // 32-bit MN-major operands use the 128-byte swizzle with 32-byte atoms
+    // (layout type 1) and 4-row K groups.
+    const uint64_t bdesc0 =
+        FMT == 2 ? (make_smem_desc(smem_base + a_bytes, BK * SWB, 4 * SWB, 0) | (1ull << 61))
+                 : make_smem_desc(smem_base + a_bytes, BK * SWB, 8 * SWB, SWB);
+    const int ksteps = BK / KSTEP;
     for (int tile = blockIdx.x; tile < num_tiles && ok; tile += tile_step, ++tcount) {
       const int buf = tcount % ACC_STAGES;
       const uint32_t use = static_cast<uint32_t>(tcount / ACC_STAGES);
@@ -169,38 +238,20 @@ __global__ void __launch_bounds__(PERSISTENT ? 256 : 128, 1)
       }
       tc_fence_after();
       const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(buf * COLS);
-      for (int kb = 0; kb < num_kb; ++kb, ++it) {
-        const int s = it % stages;
-        const uint32_t r = static_cast<uint32_t>(it / stages);
-        if (!mbar_wait(smem_u32(&sh.full[s]), r & 1u, abort_flag, err, kErrWaitMma)) {
+      for (int kb = 0; kb < num_kb; ++kb) {
+        if (!mbar_wait(smem_u32(&sh.full[s]), ph, abort_flag, err, kErrWaitMma)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        const uint32_t sa = smem_base + s * stage_bytes;
-        const uint32_t sb = sa + a_bytes;
-        const int ksteps = BK / KSTEP;
-        for (int kk = 0; kk < ksteps; ++kk) {
-          const uint32_t kbyte = static_cast<uint32_t>(kk) * 32u;
-          const uint32_t a_off = (kbyte / swa) * (BM * swa) + (kbyte % swa);
-          // MN-major B.  16-bit: 128/64/32-byte swizzle atoms of 8 K rows.
-          // tf32: 32-bit MN-major operands use the 128-byte swizzle with
-          // 32-byte atoms (layout type 1) and 4-row K groups.
-          const uint64_t bdesc =
-              FMT == 2 ? (make_smem_desc(sb + kk * KSTEP * SWB, BK * SWB, 4 * SWB, 0) |
-                          (1ull << 61))
-                       : make_smem_desc(sb + kk * KSTEP * SWB, BK * SWB, 8 * SWB, SWB);
-#pragma unroll
-          for (int h = 0; h < HALVES; ++h) {
-            const uint64_t adesc = make_smem_desc(sa + a_off + h * 128 * swa, 16, 8 * swa, swa);
-            const uint32_t acc = (kb | kk) != 0 ? 1u : 0u;
-            if constexpr (FMT == 2)
-              mma_tf32_ss(d_tmem + h * BN, adesc, bdesc, IDESC, acc);
-            else
-              mma_f16_ss(d_tmem + h * BN, adesc, bdesc, IDESC, acc);
-          }
-        }
+        const uint32_t so4 = (static_cast<uint32_t>(s) * stage_bytes) >> 4;
+        issue_kblock_any<ES, BM, SWB, HALVES, BN, FMT, false>(ksteps, d_tmem, adesc0 + so4,
+                                                              bdesc0 + so4, IDESC, kb == 0);
         mma_commit(smem_u32(&sh.empty[s]));  // stage reusable once these MMAs finish
+        if (++s == stages) {
+          s = 0;
+          ph ^= 1u;
+        }
       }
       if (!ok) break;
       mma_commit(smem_u32(&sh.acc_full[buf]));
@@ -220,7 +271,8 @@ __global__ void __launch_bounds__(PERSISTENT ? 256 : 128, 1)
     for (int tile = blockIdx.x; tile < num_tiles; tile += tile_step, ++tcount) {
       const int buf = tcount % ACC_STAGES;
       const uint32_t use = static_cast<uint32_t>(tcount / ACC_STAGES);
-      if (!mbar_wait(smem_u32(&sh.acc_full[buf]), use & 1u, abort_flag, err, kErrWaitEpilogue))
+      if (!mbar_wait_idle(smem_u32(&sh.acc_full[buf]), use & 1u, abort_flag, err,
+                          kErrWaitEpilogue))
         break;
       tc_fence_after();
       int pm, pn;
@@ -277,13 +329,22 @@ __global__ void __launch_bounds__(PERSISTENT ? 256 : 128, 1)
 }
 
 // --------------------------------------------------- CTA-pair (2-SM) tile
-// BLOCK_M = 256 with num_warps = 4: a cluster of two CTAs computes one
-// 256 x BLOCK_N tile with M=256 tcgen05 MMAs issued by the even CTA
-// (cta_group::2).  CTA r holds A rows [128r, 128r+128) and B columns
-// [r*BN/2, (r+1)*BN/2) of the tile, so each CTA stages only half of B:
-// 32 KB per 64-deep K stage for a 256x256 tile instead of 48 KB for a
-// single-CTA 128x256 tile, which lets more stages (more load latency cover)
-// fit per SM.  Each CTA's TMEM receives its own 128 rows of D.
+// BLOCK_M = 256: a cluster of two CTAs computes one 256 x BLOCK_N tile with
+// M=256 tcgen05 MMAs issued by the even CTA (cta_group::2).  CTA r holds A
+// rows [128r, 128r+128) and B columns [r*BN/2, (r+1)*BN/2) of the tile, so
+// each CTA stages only half of B: 32 KB per 64-deep K stage for a 256x256
+// tile instead of 48 KB for a single-CTA 128x256 tile, which lets more
+// stages (more load latency cover) fit per SM.  Each CTA's TMEM receives its
+// own 128 rows of D.
+//
+// num_warps 4: one tile per cluster (grid = 2 x tiles); all four warps drain
+// TMEM after the main loop.
+// num_warps 8 (PERSISTENT): one cluster per SM pair walks the tiles
+// (tile = cluster id + k x clusters, grouped raster).  Warp 0 issues TMA,
+// warp 1 of the even CTA issues MMAs, warps 4-7 of both CTAs drain TMEM;
+// two TMEM accumulator buffers let the epilogue of tile i overlap the main
+// loop of tile i+1.  The even CTA's acc_empty[b] collects the arrivals of
+// all eight epilogue warps of the pair before buffer b is overwritten.
 //
 // Barriers: full[s] lives in the even CTA only; its producer arms it with
 // the bytes of both CTAs and both producers' TMA loads count their bytes on
@@ -291,15 +352,16 @@ __global__ void __launch_bounds__(PERSISTENT ? 256 : 128, 1)
 // commits to its own and (through the cluster address) to the peer's.
 // All waits are bounded; a CTA that gives up drains and still reaches the
 // final cluster barrier, so neither CTA exits while the other can signal it.
-template <typename T, int FMT, int BN>
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(128, 1)
+template <typename T, int FMT, int BN, bool PERSISTENT>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PERSISTENT ? 256 : 128, 1)
     matmul_tc2_kernel(const __grid_constant__ CUtensorMap tma_a,
                       const __grid_constant__ CUtensorMap tma_b, T* __restrict__ C, int M, int N,
                       int K, int BK, int stages, int group_m, int swa, unsigned int* err) {
   constexpr int ES = sizeof(T);
   constexpr int BNH = BN / 2;                                 // B columns per CTA
   constexpr int SWB = (BNH * ES) < 128 ? (BNH * ES) : 128;    // B chunk width (bytes)
-  constexpr int ALLOC = BN <= 32 ? 32 : BN <= 64 ? 64 : BN <= 128 ? 128 : 256;
+  constexpr int ACC = PERSISTENT ? 2 : 1;                     // TMEM accumulator buffers
+  constexpr int ALLOC = tc2_tmem_alloc(ACC * BN);
   constexpr int KSTEP = 32 / ES;
   constexpr uint32_t IDESC = make_idesc(FMT, 256, BN, false, true);
 
@@ -314,17 +376,20 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(128, 1)
   const uint32_t rank = cluster_ctarank();
   const int num_pid_m = (M + 255) / 256;
   const int num_pid_n = (N + BN - 1) / BN;
-  const int tile = static_cast<int>(blockIdx.x >> 1);
+  const int num_tiles = num_pid_m * num_pid_n;
+  const int first_tile = static_cast<int>(blockIdx.x >> 1);
+  const int tile_step = PERSISTENT ? static_cast<int>(gridDim.x >> 1) : num_tiles;
   const int num_kb = (K + BK - 1) / BK;
-  int pm, pn;
-  tile_coords(tile, num_pid_m, num_pid_n, group_m, pm, pn);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < stages; ++s) {
       mbar_init(smem_u32(&sh.full[s]), 1);
       mbar_init(smem_u32(&sh.empty[s]), 1);
     }
-    mbar_init(smem_u32(&sh.acc_full[0]), 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(smem_u32(&sh.acc_full[b]), 1);
+      mbar_init(smem_u32(&sh.acc_empty[b]), 8);  // 4 epilogue warps x 2 CTAs
+    }
     mbar_init(smem_u32(&sh.drain), 1);
     sh.abort = 0;
     fence_barrier_init();
@@ -344,28 +409,34 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(128, 1)
   if (warp == 0 && lane == 0) {
     // ------------------------------------------------------ producers (both)
     const uint32_t full0 = mapa_shared(smem_u32(&sh.full[0]), 0);  // even CTA's full[0]
-    int it = 0;
+    int it = 0, s = 0;  // K blocks issued; ring slot and phase of the next one
+    uint32_t ph = 0;
     bool ok = true;
-    for (int kb = 0; kb < num_kb; ++kb, ++it) {
-      const int s = it % stages;
-      const uint32_t r = static_cast<uint32_t>(it / stages);
-      if (!mbar_wait(smem_u32(&sh.empty[s]), (r & 1u) ^ 1u, abort_flag, err,
-                     kErrWaitProducer)) {
-        ok = false;
-        break;
-      }
-      const uint32_t full = full0 + static_cast<uint32_t>(s) * 8u;
-      if (rank == 0) mbar_arrive_expect_tx(smem_u32(&sh.full[s]), 2u * (a_bytes + b_bytes));
-      const uint32_t sa = smem_base + s * stage_bytes;
-      const uint32_t sb = sa + a_bytes;
-      const int a_atoms = (BK * ES) / swa;
-      for (int a = 0; a < a_atoms; ++a)
-        tma_load_2d_pair(sa + a * 128 * swa, &tma_a, full, kb * BK + a * (swa / ES),
-                         pm * 256 + static_cast<int>(rank) * 128);
+    for (int tile = first_tile; tile < num_tiles && ok; tile += tile_step) {
+      int pm, pn;
+      tile_coords(tile, num_pid_m, num_pid_n, group_m, pm, pn);
+      for (int kb = 0; kb < num_kb; ++kb, ++it) {
+        if (!mbar_wait(smem_u32(&sh.empty[s]), ph ^ 1u, abort_flag, err, kErrWaitProducer)) {
+          ok = false;
+          break;
+        }
+        const uint32_t full = full0 + static_cast<uint32_t>(s) * 8u;
+        if (rank == 0) mbar_arrive_expect_tx(smem_u32(&sh.full[s]), 2u * (a_bytes + b_bytes));
+        const uint32_t sa = smem_base + s * stage_bytes;
+        const uint32_t sb = sa + a_bytes;
+        const int a_atoms = (BK * ES) / swa;
+        for (int a = 0; a < a_atoms; ++a)
+          tma_load_2d_pair(sa + a * 128 * swa, &tma_a, full, kb * BK + a * (swa / ES),
+                           pm * 256 + static_cast<int>(rank) * 128);
 #pragma unroll
-      for (int c = 0; c < (BNH * ES) / SWB; ++c)
-        tma_load_2d_pair(sb + c * BK * SWB, &tma_b, full,
-                         pn * BN + static_cast<int>(rank) * BNH + c * (SWB / ES), kb * BK);
+        for (int c = 0; c < (BNH * ES) / SWB; ++c)
+          tma_load_2d_pair(sb + c * BK * SWB, &tma_b, full,
+                           pn * BN + static_cast<int>(rank) * BNH + c * (SWB / ES), kb * BK);
+        if (++s == stages) {
+          s = 0;
+          ph ^= 1u;
+        }
+      }
     }
     if (!ok) {
       if (rank == 0) {
@@ -382,56 +453,75 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(128, 1)
   } else if (warp == 1 && lane == 0 && rank == 0) {
     // --------------------------------------------- MMA issuer (even CTA)
     const uint32_t peer_empty0 = mapa_shared(smem_u32(&sh.empty[0]), 1);
-    const uint32_t peer_acc = mapa_shared(smem_u32(&sh.acc_full[0]), 1);
-    int it = 0;
+    const uint32_t peer_acc0 = mapa_shared(smem_u32(&sh.acc_full[0]), 1);
+    int tcount = 0, s = 0;  // ring slot and phase of the next K block
+    uint32_t ph = 0;
     bool ok = true;
-    for (int kb = 0; kb < num_kb; ++kb, ++it) {
-      const int s = it % stages;
-      const uint32_t r = static_cast<uint32_t>(it / stages);
-      if (!mbar_wait(smem_u32(&sh.full[s]), r & 1u, abort_flag, err, kErrWaitMma)) {
+    // slot-0 / K-step-0 descriptors; slots and K steps add to the start
+    // address field only (see matmul_tc_kernel)
+    const uint64_t adesc0 = make_smem_desc(smem_base, 16, 8 * swa, swa);
+    const uint64_t bdesc0 =
+        FMT == 2 ? (make_smem_desc(smem_base + a_bytes, BK * SWB, 4 * SWB, 0) | (1ull << 61))
+                 : make_smem_desc(smem_base + a_bytes, BK * SWB, 8 * SWB, SWB);
+    const int ksteps = BK / KSTEP;
+    for (int tile = first_tile; tile < num_tiles && ok; tile += tile_step, ++tcount) {
+      const int buf = tcount % ACC;
+      const uint32_t use = static_cast<uint32_t>(tcount / ACC);
+      if (PERSISTENT && !mbar_wait<true>(smem_u32(&sh.acc_empty[buf]), (use & 1u) ^ 1u,
+                                         abort_flag, err, kErrWaitMma)) {
         ok = false;
         break;
       }
       tc_fence_after();
-      const uint32_t sa = smem_base + s * stage_bytes;
-      const uint32_t sb = sa + a_bytes;
-      for (int kk = 0; kk < BK / KSTEP; ++kk) {
-        const uint32_t kbyte = static_cast<uint32_t>(kk) * 32u;
-        const uint64_t adesc =
-            make_smem_desc(sa + (kbyte / swa) * (128 * swa) + (kbyte % swa), 16, 8 * swa, swa);
-        const uint64_t bdesc =
-            FMT == 2 ? (make_smem_desc(sb + kk * KSTEP * SWB, BK * SWB, 4 * SWB, 0) |
-                        (1ull << 61))
-                     : make_smem_desc(sb + kk * KSTEP * SWB, BK * SWB, 8 * SWB, SWB);
-        const uint32_t acc = (kb | kk) != 0 ? 1u : 0u;
-        if constexpr (FMT == 2)
-          mma_tf32_ss_pair(tmem_base, adesc, bdesc, IDESC, acc);
-        else
-          mma_f16_ss_pair(tmem_base, adesc, bdesc, IDESC, acc);
+      const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(buf * BN);
+      for (int kb = 0; kb < num_kb; ++kb) {
+        if (!mbar_wait(smem_u32(&sh.full[s]), ph, abort_flag, err, kErrWaitMma)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t so4 = (static_cast<uint32_t>(s) * stage_bytes) >> 4;
+        issue_kblock_any<ES, 128, SWB, 1, BN, FMT, true>(ksteps, d_tmem, adesc0 + so4,
+                                                         bdesc0 + so4, IDESC, kb == 0);
+        mma_commit_pair(smem_u32(&sh.empty[s]));
+        mma_commit_pair(peer_empty0 + static_cast<uint32_t>(s) * 8u);
+        if (++s == stages) {
+          s = 0;
+          ph ^= 1u;
+        }
       }
-      mma_commit_pair(smem_u32(&sh.empty[s]));
-      mma_commit_pair(peer_empty0 + static_cast<uint32_t>(s) * 8u);
+      if (!ok) break;
+      mma_commit_pair(smem_u32(&sh.acc_full[buf]));
+      mma_commit_pair(peer_acc0 + static_cast<uint32_t>(buf) * 8u);
     }
-    if (ok) {
-      mma_commit_pair(smem_u32(&sh.acc_full[0]));
-      mma_commit_pair(peer_acc);
-    } else {
+    if (!ok) {
       mma_commit_pair(smem_u32(&sh.drain));
       mbar_wait_drain(smem_u32(&sh.drain), 0, err);
     }
   }
 
   // ------------------------------------------------------- epilogue (both)
-  __syncwarp();
-  {
+  const bool epi_warp = PERSISTENT ? (warp >= 4) : true;
+  if (epi_warp) {
+    __syncwarp();
     const int q = warp & 3;
-    if (mbar_wait(smem_u32(&sh.acc_full[0]), 0, abort_flag, err, kErrWaitEpilogue)) {
+    const uint32_t leader_acc_empty0 = mapa_shared(smem_u32(&sh.acc_empty[0]), 0);
+    int tcount = 0;
+    for (int tile = first_tile; tile < num_tiles; tile += tile_step, ++tcount) {
+      const int buf = tcount % ACC;
+      const uint32_t use = static_cast<uint32_t>(tcount / ACC);
+      if (!mbar_wait_idle(smem_u32(&sh.acc_full[buf]), use & 1u, abort_flag, err,
+                          kErrWaitEpilogue))
+        break;
       tc_fence_after();
+      int pm, pn;
+      tile_coords(tile, num_pid_m, num_pid_n, group_m, pm, pn);
       const int row = pm * 256 + static_cast<int>(rank) * 128 + q * 32 + lane;
 #pragma unroll 1
       for (int c = 0; c < BN / 32; ++c) {
         uint32_t r[32];
-        tmem_ld32(tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(c * 32),
+        tmem_ld32(tmem_base + (static_cast<uint32_t>(q * 32) << 16) +
+                      static_cast<uint32_t>(buf * BN + c * 32),
                   r);
         tmem_wait_ld();
         const int col0 = pn * BN + c * 32;
@@ -461,6 +551,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(128, 1)
               if (col0 + i < N) dst[i] = Elem<T>::from_f(__uint_as_float(r[i]));
           }
         }
+      }
+      if (PERSISTENT) {
+        // this warp's TMEM rows of buffer buf are read: free them for the
+        // MMA issuer of the pair (even CTA)
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive_cluster(leader_acc_empty0 + static_cast<uint32_t>(buf) * 8u);
       }
     }
   }
@@ -542,12 +639,13 @@ gpo_status plan_matmul_tc(const gpo_key& k, Plan& p, std::string& log) {
   // BLOCK_M 256 with 4 warps: a CTA pair (cta_group::2), each CTA staging
   // 128 rows of A and BLOCK_N/2 columns of B.  tf32 needs the 128-byte B
   // chunk (BLOCK_N/2 * 4 >= 128) for its 32-bit MN-major layout.
-  const bool pair = BM == 256 && k.num_warps == 4 && (k.dtype != GPO_TF32 || BN >= 64);
+  // With 8 warps the pair is persistent (one cluster per SM pair walking
+  // the tiles, two TMEM accumulator buffers).
+  const bool pair = BM == 256 && (k.dtype != GPO_TF32 || BN >= 64);
   if (pair) {
     const uint32_t pa = 128u * BK * es, pb = static_cast<uint32_t>(BK) * (BN / 2) * es;
     const uint32_t pst = (pa + pb + 1023u) & ~1023u;
-    int pc = 32;
-    while (pc < BN) pc *= 2;
+    const int pc = tc2_tmem_alloc((persistent ? 2 : 1) * BN);
     // Never let more CTAs share an SM than its 512 TMEM columns hold: a pair
     // allocation that had to wait on one SM of the pair while holding the
     // other could otherwise wait on a second pair doing the opposite.  The
@@ -564,17 +662,20 @@ gpo_status plan_matmul_tc(const gpo_key& k, Plan& p, std::string& log) {
     }
     p.aux[0] = std::min(BK * es, 128);
     p.aux[1] = static_cast<int>(pdyn);
-    p.aux[2] = 0;
+    p.aux[2] = persistent ? 1 : 0;
     p.aux[3] = 1;  // pair
     p.family = "matmul_tc";
     p.res.smem_bytes = psmem;
     p.res.tmem_cols = static_cast<uint32_t>(pc);
-    p.res.threads_per_cta = 128u;
+    p.res.threads_per_cta = persistent ? 256u : 128u;
+    // persistent: clamped to the co-resident cluster count at launch
     p.res.grid_x = static_cast<uint32_t>(2 * cdiv(M, 256) * cdiv(N, BN));
     p.res.grid_y = p.res.grid_z = 1;
+    p.res.persistent = persistent ? 1u : 0u;
     p.res.launches_per_call = 1;
     const char* tn = k.dtype == GPO_BFLOAT16 ? "bf16" : k.dtype == GPO_FLOAT16 ? "f16" : "tf32";
-    snprintf(p.res.kernel, sizeof(p.res.kernel), "matmul_tc2_kernel<%s,256,%d,cta_pair>", tn, BN);
+    snprintf(p.res.kernel, sizeof(p.res.kernel), "matmul_tc2_kernel<%s,256,%d,cta_pair%s>", tn,
+             BN, persistent ? "_persistent" : "");
     return GPO_OK;
   }
   p.aux[3] = 0;
@@ -639,7 +740,7 @@ static gpo_status run_tc(const gpo_key& k, const Plan& p, const gpo_args& a, con
   return launch_status();
 }
 
-template <typename T, int FMT, int BN>
+template <typename T, int FMT, int BN, bool P>
 static gpo_status run_tc2(const gpo_key& k, const Plan& p, const gpo_args& a, const LaunchCtx& c,
                           CUtensorMapDataType dt) {
   const int es = sizeof(T);
@@ -651,12 +752,16 @@ static gpo_status run_tc2(const gpo_key& k, const Plan& p, const gpo_args& a, co
   if (!encode_2d(&ma, dt, a.in[0], M, K, es, swa / es, 128, swa)) return GPO_LAUNCH_ERROR;
   if (!encode_2d(&mb, dt, a.in[1], K, N, es, SWB / es, k.block_k, SWB, FMT == 2))
     return GPO_LAUNCH_ERROR;
-  auto kern = matmul_tc2_kernel<T, FMT, BN>;
+  auto kern = matmul_tc2_kernel<T, FMT, BN, P>;
   const uint32_t dyn = static_cast<uint32_t>(p.aux[1]);
   gpo_status s = ensure_smem_attr(reinterpret_cast<const void*>(kern), dyn);
   if (s != GPO_OK) return s;
-  const unsigned grid = static_cast<unsigned>(2 * cdiv(M, 256) * cdiv(N, BN));
-  kern<<<grid, 128, dyn, c.stream>>>(ma, mb, static_cast<T*>(a.out), static_cast<int>(M),
+  const int64_t tiles = cdiv(M, 256) * cdiv(N, BN);
+  const int threads = P ? 256 : 128;
+  const unsigned grid =
+      2u * (P ? persistent_clusters(reinterpret_cast<const void*>(kern), threads, dyn, tiles)
+              : static_cast<unsigned>(tiles));
+  kern<<<grid, threads, dyn, c.stream>>>(ma, mb, static_cast<T*>(a.out), static_cast<int>(M),
                                      static_cast<int>(N), static_cast<int>(K), k.block_k,
                                      k.num_stages, k.group_m, swa, c.err);
   return launch_status();
@@ -665,11 +770,16 @@ static gpo_status run_tc2(const gpo_key& k, const Plan& p, const gpo_args& a, co
 template <typename T, int FMT>
 static gpo_status run_tc2_bn(const gpo_key& k, const Plan& p, const gpo_args& a,
                              const LaunchCtx& c, CUtensorMapDataType dt) {
+  const bool P = p.aux[2] != 0;
   switch (k.block_n) {
-    case 32: return run_tc2<T, FMT, 32>(k, p, a, c, dt);
-    case 64: return run_tc2<T, FMT, 64>(k, p, a, c, dt);
-    case 128: return run_tc2<T, FMT, 128>(k, p, a, c, dt);
-    case 256: return run_tc2<T, FMT, 256>(k, p, a, c, dt);
+    case 32: return P ? run_tc2<T, FMT, 32, true>(k, p, a, c, dt)
+                      : run_tc2<T, FMT, 32, false>(k, p, a, c, dt);
+    case 64: return P ? run_tc2<T, FMT, 64, true>(k, p, a, c, dt)
+                      : run_tc2<T, FMT, 64, false>(k, p, a, c, dt);
+    case 128: return P ? run_tc2<T, FMT, 128, true>(k, p, a, c, dt)
+                       : run_tc2<T, FMT, 128, false>(k, p, a, c, dt);
+    case 256: return P ? run_tc2<T, FMT, 256, true>(k, p, a, c, dt)
+                       : run_tc2<T, FMT, 256, false>(k, p, a, c, dt);
     default: return GPO_INTERNAL;
   }
 }

@@ -50,9 +50,10 @@ MM_TC = [  # tcgen05 family: (BM, BN, BK, GROUP_M, warps, stages)
     (128, 32, 32, 1, 4, 2), (128, 64, 64, 4, 8, 3), (128, 128, 64, 8, 8, 4),
     (128, 256, 64, 8, 8, 4), (128, 256, 128, 1, 4, 2), (256, 128, 64, 4, 8, 3),
     (256, 256, 64, 16, 8, 2), (256, 64, 32, 1, 4, 5), (128, 128, 256, 4, 8, 2),
-    # CTA pairs (cta_group::2)
+    # CTA pairs (cta_group::2); 8 warps -> persistent pairs
     (256, 256, 64, 8, 4, 3), (256, 128, 64, 4, 4, 3), (256, 32, 32, 1, 4, 2),
-    (256, 256, 128, 8, 4, 2),
+    (256, 256, 128, 8, 4, 2), (256, 256, 64, 8, 8, 6), (256, 128, 64, 16, 8, 8),
+    (256, 64, 64, 1, 8, 4),
 ]
 MM_SIMT = [(16, 16, 16, 1, 2, 2), (32, 32, 16, 1, 4, 2), (64, 128, 32, 4, 8, 3),
            (128, 128, 64, 8, 8, 4)]
@@ -145,8 +146,9 @@ def test_parity_new_variants_with_oracle(name, dtype):
         assert_close(name, dtype, out, ref, f"{cfg} [{kc.launch['kernel']}]")
 
 
+# (2048, 2560, 256) gives persistent clusters several tiles each
 MM_SHAPES = [(384, 320, 288), (1000, 1000, 1000), (257, 512, 136), (128, 256, 64),
-             (1024, 2048, 512)]
+             (1024, 2048, 512), (2048, 2560, 256)]
 
 
 @pytest.mark.parametrize("dtype", ["bfloat16", "float16", "tf32"])
