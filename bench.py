@@ -36,8 +36,8 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 SHAPE = (4096, 4096, 4096)
-BEST = {"BLOCK_M": 128, "BLOCK_N": 256, "BLOCK_K": 64, "GROUP_M": 8, "num_warps": 4,
-        "num_stages": 2, "dtype": "bfloat16"}
+BEST = {"BLOCK_M": 256, "BLOCK_N": 256, "BLOCK_K": 64, "GROUP_M": 16, "num_warps": 4,
+        "num_stages": 3, "dtype": "bfloat16"}
 FLOPS = 2.0 * SHAPE[0] * SHAPE[1] * SHAPE[2]
 N_SETS = 4
 METRIC = "matmul_bf16_4096_tflops"

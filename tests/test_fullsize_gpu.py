@@ -10,11 +10,19 @@ from oracle import reference as O
 
 pytestmark = pytest.mark.gpu
 
-MM_BEST = {"BLOCK_M": 128, "BLOCK_N": 256, "BLOCK_K": 64, "GROUP_M": 8, "num_warps": 8,
-           "num_stages": 4, "dtype": "bfloat16"}
+# the headline CTA-pair tile, the persistent CTA pair and the persistent 1-CTA tile
+MM_FULL = [
+    {"BLOCK_M": 256, "BLOCK_N": 256, "BLOCK_K": 64, "GROUP_M": 16, "num_warps": 4,
+     "num_stages": 3, "dtype": "bfloat16"},
+    {"BLOCK_M": 256, "BLOCK_N": 256, "BLOCK_K": 64, "GROUP_M": 16, "num_warps": 8,
+     "num_stages": 6, "dtype": "bfloat16"},
+    {"BLOCK_M": 128, "BLOCK_N": 256, "BLOCK_K": 64, "GROUP_M": 8, "num_warps": 8,
+     "num_stages": 4, "dtype": "bfloat16"},
+]
 
 
-def test_matmul_4096_linearity_and_reference():
+@pytest.mark.parametrize("MM_BEST", MM_FULL, ids=lambda c: f"{c['BLOCK_M']}x{c['BLOCK_N']}w{c['num_warps']}")
+def test_matmul_4096_linearity_and_reference(MM_BEST):
     task = get_task("matmul", "b200")
     shape = (4096, 4096, 4096)
     a, b = task.make_inputs(shape, "bfloat16", "cuda", 0)
