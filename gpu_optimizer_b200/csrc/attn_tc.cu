@@ -5,7 +5,7 @@
 // inputs with BLOCK_M = 128.  One CTA per (128-row query tile, batch*head);
 // causal grids visit the longest query tiles first.
 //
-// Warp roles (num_warps 4 -> 8 warps):
+// Warp roles:
 //   warp 0  TMA producer of Q (once) and of the K ring (num_stages slots).
 //   warp 3  TMA producer of the V ring (num_stages slots).  K slot j is
 //           released when S_j's MMAs complete, V slot j when PV_j's do, so
@@ -16,24 +16,26 @@
 //                         PV MMAs, so the softmax of block j overlaps the
 //                         MMAs of S_{j+1}, S_{j+2} and PV_{j-1}.
 //   warp 2  TMEM owner.
-//   warps 4-7 softmax / correction / epilogue: thread r owns query row r
-//           (TMEM lane r).  It reads S_j from TMEM, applies scale, padding
-//           and causal masks, keeps the running max in the log2 domain,
-//           writes P_j = exp2(s - m) as 16-bit pairs back into TMEM over its
-//           own S buffer (the A operand of the PV MMA, read from TMEM) and
-//           accumulates the fp32 row sum.  Scale/shift FMAs and row-sum adds
+//   softmax warpgroups (WG = 1 with num_warps 4: warps 4-7; WG = 2 with
+//           num_warps 8: warps 4-7 and 8-11): query row r is TMEM lane r,
+//           read by warp 4 + r/32 (and 8 + r/32).  With WG = 2 the two
+//           warps of a row each take half of the block's columns and of
+//           O's columns, exchanging their partial row max through shared
+//           memory once per block (a 64-thread named barrier per warp
+//           pair), so every SM sub-partition runs two softmax warps and one
+//           warp's TMEM / barrier latency hides behind the other's math.
+//           Per block: read S_j from TMEM, apply scale, padding and causal
+//           masks, keep the running max in the log2 domain, write
+//           P_j = exp2(s - m) as 16-bit pairs back into TMEM over the same
+//           S buffer (the A operand of the PV MMA, read from TMEM) and
+//           accumulate the fp32 row sum.  Scale/shift FMAs and row-sum adds
 //           run as packed fp32x2 operations and the row max as three-input
-//           max, so the exp2 on the MUFU unit dominates the instruction mix.
-//           The running max used for P is only moved (and O in TMEM
+//           max.  The running max used for P is only moved (and O in TMEM
 //           rescaled) when a block's max exceeds it by more than 8 (a factor
 //           of 256); until then P <= 256, which 16-bit P and the fp32
 //           accumulator represent exactly as well as P <= 1.
-// num_warps 8 doubles the CTA: two softmax warpgroups (warps 4-7 and 8-11),
-// each owning its own 128-row query tile, share every K/V tile; the MMA
-// issuer interleaves both tiles' S and PV MMAs.
-// TMEM columns per tile t of NT: O_t [t*D, t*D+D), S/P buffers
-// [NT*D + (NB*t+b)*BN, +BN) for b < NB; NB = 3 when NT*(D + 3*BN) <= 512,
-// else 2.
+// TMEM columns: O [0, D), S/P buffers [D + b*BN, D + (b+1)*BN) for b < NB;
+// NB = 3 when D + 3*BN <= 512, else 2.
 #include <algorithm>
 
 #include "gpo_common.cuh"
@@ -43,14 +45,10 @@ namespace gpo {
 
 constexpr int kAttnMaxStages = 4;
 constexpr float kRescaleThreshold = 8.0f;
+constexpr int kAttnMaxSBufs = 3;  // S/P buffers
 
-constexpr int kAttnMaxTiles = 2;  // query tiles (softmax warpgroups) per CTA
-constexpr int kAttnMaxSBufs = 3;  // S/P buffers per query tile
-
-// S/P buffers per query tile: three when TMEM has room, else two.
-__host__ __device__ constexpr int attn_sbufs(int nt, int d, int bn) {
-  return nt * (d + 3 * bn) <= 512 ? 3 : 2;
-}
+// S/P buffers: three when TMEM has room, else two.
+__host__ __device__ constexpr int attn_sbufs(int d, int bn) { return d + 3 * bn <= 512 ? 3 : 2; }
 
 struct AttnShared {
   uint64_t q_full;
@@ -58,13 +56,18 @@ struct AttnShared {
   uint64_t k_empty[kAttnMaxStages];
   uint64_t v_full[kAttnMaxStages];
   uint64_t v_empty[kAttnMaxStages];
-  uint64_t s_full[kAttnMaxTiles][kAttnMaxSBufs];
-  uint64_t p_full[kAttnMaxTiles][kAttnMaxSBufs];
-  uint64_t pv_done[kAttnMaxTiles][kAttnMaxSBufs];
+  uint64_t s_full[kAttnMaxSBufs];
+  uint64_t p_full[kAttnMaxSBufs];
+  uint64_t pv_done[kAttnMaxSBufs];
   uint64_t drain;
   uint32_t tmem_base;
   int abort;
 };
+
+// WG = 2 exchange area after the V ring in dynamic shared memory:
+// [block parity][warpgroup][row] partial row maxima; the epilogue's partial
+// row sums reuse the parity slot the last block did not read.
+constexpr uint32_t kAttnXchgBytes = 2u * 2u * 128u * sizeof(float);
 
 __host__ __device__ constexpr int attn_tmem_alloc(int cols) {
   return cols <= 32 ? 32 : cols <= 64 ? 64 : cols <= 128 ? 128 : cols <= 256 ? 256 : 512;
@@ -76,8 +79,29 @@ __device__ __forceinline__ float fmax3(float a, float b, float c) {
   return d;
 }
 
-template <typename T, int FMT, int BN, int D, bool CAUSAL, int NT>
-__global__ void __launch_bounds__(NT == 1 ? 256 : 384, 1)
+// Barrier `id` (1..15) among `count` threads (whole warps).
+__device__ __forceinline__ void named_barrier(uint32_t id, uint32_t count) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+
+// TMEM load / store of C consecutive 32-bit columns (C = 16 or 32).
+template <int C>
+__device__ __forceinline__ void tmem_ld_cols(uint32_t taddr, uint32_t* r) {
+  if constexpr (C == 32)
+    tmem_ld32(taddr, *reinterpret_cast<uint32_t(*)[32]>(r));
+  else
+    tmem_ld16(taddr, r);
+}
+template <int C>
+__device__ __forceinline__ void tmem_st_cols(uint32_t taddr, const uint32_t* r) {
+  if constexpr (C == 32)
+    tmem_st32(taddr, *reinterpret_cast<const uint32_t(*)[32]>(r));
+  else
+    tmem_st16(taddr, r);
+}
+
+template <typename T, int FMT, int BN, int D, bool CAUSAL, int WG>
+__global__ void __launch_bounds__(128 + 128 * WG, 1)
     attn_tc_kernel(const __grid_constant__ CUtensorMap tma_q,
                    const __grid_constant__ CUtensorMap tma_k,
                    const __grid_constant__ CUtensorMap tma_v, T* __restrict__ O, int S,
@@ -87,36 +111,36 @@ __global__ void __launch_bounds__(NT == 1 ? 256 : 384, 1)
   constexpr uint32_t Q_BYTES = 128u * D * ES;
   constexpr uint32_t KV_BYTES = static_cast<uint32_t>(BN) * D * ES;
   constexpr uint32_t KV_SLOT = (KV_BYTES + 1023u) & ~1023u;
-  constexpr int NB = attn_sbufs(NT, D, BN);
+  constexpr int NB = attn_sbufs(D, BN);
   constexpr int LAG = NB - 1;  // S MMAs run LAG blocks ahead of PV MMAs
-  constexpr int COLS = NT * D + NT * NB * BN;
+  constexpr int COLS = D + NB * BN;
   constexpr int ALLOC = attn_tmem_alloc(COLS);
   constexpr uint32_t IDESC_S = make_idesc(FMT, 128, BN, false, false);
   constexpr uint32_t IDESC_O = make_idesc(FMT, 128, D, false, true);
+  constexpr int SC = BN / WG;        // S columns per softmax warp
+  constexpr int OC = D / WG;         // O columns per softmax warp
+  constexpr int SCH = SC < 32 ? SC : 32;  // TMEM access chunk (S)
+  constexpr int OCH = OC < 32 ? OC : 32;  // TMEM access chunk (O)
   static_assert(COLS <= 512, "TMEM holds 512 columns");
+  static_assert(SC >= 32 && OC >= 16, "softmax warps need >= 32 S and >= 16 O columns");
 
   __shared__ AttnShared sh;
   extern __shared__ uint8_t dyn_smem[];
   const uint32_t base = (smem_u32(dyn_smem) + 1023u) & ~1023u;
-  const uint32_t q_smem = base;  // NT tiles
-  const uint32_t k_smem = q_smem + NT * Q_BYTES;
+  const uint32_t q_smem = base;
+  const uint32_t k_smem = q_smem + Q_BYTES;
   const uint32_t v_smem = k_smem + static_cast<uint32_t>(stages) * KV_SLOT;
+  float* xchg = reinterpret_cast<float*>(
+      dyn_smem + (v_smem + static_cast<uint32_t>(stages) * KV_SLOT - smem_u32(dyn_smem)));
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  constexpr int CTA_ROWS = 128 * NT;
-  const int num_q_tiles = (S + CTA_ROWS - 1) / CTA_ROWS;
+  const int num_q_tiles = (S + 127) / 128;
   // longest causal rows first; identity order for the non-causal task
   const int qt = CAUSAL ? (num_q_tiles - 1 - static_cast<int>(blockIdx.x))
                         : static_cast<int>(blockIdx.x);
-  const int q0 = qt * CTA_ROWS;
+  const int q0 = qt * 128;
   const int bh = blockIdx.y;
-  // KV blocks query tile t needs (causal tiles stop at their diagonal);
-  // computed, not indexed from an array, so it never lands in local memory
-  auto nblk_of = [&](int t) -> int {
-    const int kv_len = CAUSAL ? min(S, q0 + 128 * t + 128) : S;
-    return (kv_len + BN - 1) / BN;
-  };
-  const int nblk_max = nblk_of(NT - 1);
+  const int nblk = ((CAUSAL ? min(S, q0 + 128) : S) + BN - 1) / BN;  // causal: stop at diagonal
 
   if (threadIdx.x == 0) {
     mbar_init(smem_u32(&sh.q_full), 1);
@@ -126,12 +150,11 @@ __global__ void __launch_bounds__(NT == 1 ? 256 : 384, 1)
       mbar_init(smem_u32(&sh.v_full[s]), 1);
       mbar_init(smem_u32(&sh.v_empty[s]), 1);
     }
-    for (int t = 0; t < NT; ++t)
-      for (int b = 0; b < NB; ++b) {
-        mbar_init(smem_u32(&sh.s_full[t][b]), 1);
-        mbar_init(smem_u32(&sh.p_full[t][b]), 4);
-        mbar_init(smem_u32(&sh.pv_done[t][b]), 1);
-      }
+    for (int b = 0; b < NB; ++b) {
+      mbar_init(smem_u32(&sh.s_full[b]), 1);
+      mbar_init(smem_u32(&sh.p_full[b]), 4 * WG);
+      mbar_init(smem_u32(&sh.pv_done[b]), 1);
+    }
     mbar_init(smem_u32(&sh.drain), 1);
     sh.abort = 0;
     fence_barrier_init();
@@ -156,22 +179,19 @@ __global__ void __launch_bounds__(NT == 1 ? 256 : 384, 1)
     const uint32_t ring = is_k ? k_smem : v_smem;
     uint64_t* full = is_k ? sh.k_full : sh.v_full;
     uint64_t* empty = is_k ? sh.k_empty : sh.v_empty;
-    const uint32_t site = kErrWaitProducer;
     bool ok = true;
     int issued = 0;
     if (is_k) {
-      mbar_arrive_expect_tx(smem_u32(&sh.q_full), NT * Q_BYTES);
+      mbar_arrive_expect_tx(smem_u32(&sh.q_full), Q_BYTES);
 #pragma unroll
-      for (int t = 0; t < NT; ++t)
-#pragma unroll
-        for (int a = 0; a < (D * ES) / SWQ; ++a)
-          tma_load_3d(q_smem + t * Q_BYTES + a * 128 * SWQ, &tma_q, smem_u32(&sh.q_full),
-                      a * (SWQ / ES), q0 + 128 * t, bh);
+      for (int a = 0; a < (D * ES) / SWQ; ++a)
+        tma_load_3d(q_smem + a * 128 * SWQ, &tma_q, smem_u32(&sh.q_full), a * (SWQ / ES), q0,
+                    bh);
     }
-    for (int j = 0; j < nblk_max; ++j) {
+    for (int j = 0; j < nblk; ++j) {
       const int s = j % stages;
       const uint32_t r = static_cast<uint32_t>(j / stages);
-      if (!mbar_wait(smem_u32(&empty[s]), (r & 1u) ^ 1u, abort_flag, err, site)) {
+      if (!mbar_wait(smem_u32(&empty[s]), (r & 1u) ^ 1u, abort_flag, err, kErrWaitProducer)) {
         ok = false;
         break;
       }
@@ -191,35 +211,29 @@ __global__ void __launch_bounds__(NT == 1 ? 256 : 384, 1)
   } else if (warp == 1 && lane == 0) {
     // ---------------------------------------------------------- MMA issuer
     bool ok = mbar_wait(smem_u32(&sh.q_full), 0, abort_flag, err, kErrWaitMma);
-    // O_t += P_t(i) V(i) for every tile that still needs block i, then
-    // release V slot i.
+    // O += P(i) V(i), then release V slot i.
     auto pv_round = [&](int i) -> bool {
       const int s = i % stages;
       const uint32_t r = static_cast<uint32_t>(i / stages);
       const int b = i % NB;
       const uint32_t u = static_cast<uint32_t>(i / NB);
       if (!mbar_wait(smem_u32(&sh.v_full[s]), r & 1u, abort_flag, err, kErrWaitMma)) return false;
+      if (!mbar_wait(smem_u32(&sh.p_full[b]), u & 1u, abort_flag, err, kErrWaitMma)) return false;
+      tc_fence_after();
       const uint32_t vs = v_smem + static_cast<uint32_t>(s) * KV_SLOT;
+      // P(i) sits in the first BN/2 columns of S/P buffer b (16-bit pairs)
+      const uint32_t pa = tmem + static_cast<uint32_t>(D + b * BN);
 #pragma unroll
-      for (int t = 0; t < NT; ++t) {
-        if (i >= nblk_of(t)) continue;
-        if (!mbar_wait(smem_u32(&sh.p_full[t][b]), u & 1u, abort_flag, err, kErrWaitMma))
-          return false;
-        tc_fence_after();
-        // P_t(i) sits in the first BN/2 columns of S/P buffer b (16-bit pairs)
-        const uint32_t pa = tmem + static_cast<uint32_t>(NT * D + (t * NB + b) * BN);
-#pragma unroll
-        for (int kk = 0; kk < BN / 16; ++kk) {
-          const uint64_t bdesc = make_smem_desc(vs + kk * 16 * SWQ, BN * SWQ, 8 * SWQ, SWQ);
-          mma_f16_ts(tmem + static_cast<uint32_t>(t * D), pa + static_cast<uint32_t>(kk * 8),
-                     bdesc, IDESC_O, (i > 0 || kk > 0) ? 1u : 0u);
-        }
-        mma_commit(smem_u32(&sh.pv_done[t][b]));
+      for (int kk = 0; kk < BN / 16; ++kk) {
+        const uint64_t bdesc = make_smem_desc(vs + kk * 16 * SWQ, BN * SWQ, 8 * SWQ, SWQ);
+        mma_f16_ts(tmem, pa + static_cast<uint32_t>(kk * 8), bdesc, IDESC_O,
+                   (i > 0 || kk > 0) ? 1u : 0u);
       }
+      mma_commit(smem_u32(&sh.pv_done[b]));
       mma_commit(smem_u32(&sh.v_empty[s]));
       return true;
     };
-    for (int j = 0; j < nblk_max && ok; ++j) {
+    for (int j = 0; j < nblk && ok; ++j) {
       const int s = j % stages;
       const uint32_t r = static_cast<uint32_t>(j / stages);
       const int b = j % NB;
@@ -229,88 +243,94 @@ __global__ void __launch_bounds__(NT == 1 ? 256 : 384, 1)
       }
       tc_fence_after();
       const uint32_t ks = k_smem + static_cast<uint32_t>(s) * KV_SLOT;
+      // Buffer b last held P(j - NB), whose PV MMA this thread issued
+      // earlier; tcgen05 MMAs of one thread execute in issue order.
+      const uint32_t s_tmem = tmem + static_cast<uint32_t>(D + b * BN);
 #pragma unroll
-      for (int t = 0; t < NT; ++t) {
-        if (j >= nblk_of(t)) continue;
-        // Buffer b last held P_t(j - NB), whose PV MMA this thread issued
-        // earlier; tcgen05 MMAs of one thread execute in issue order.
-        const uint32_t s_tmem = tmem + static_cast<uint32_t>(NT * D + (t * NB + b) * BN);
-        const uint32_t qs = q_smem + t * Q_BYTES;
-#pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk) {
-          const uint32_t kbyte = static_cast<uint32_t>(kk) * 32u;
-          const uint32_t aoff = (kbyte / SWQ) * (128 * SWQ) + (kbyte % SWQ);
-          const uint32_t boff = (kbyte / SWQ) * (BN * SWQ) + (kbyte % SWQ);
-          const uint64_t adesc = make_smem_desc(qs + aoff, 16, 8 * SWQ, SWQ);
-          const uint64_t bdesc = make_smem_desc(ks + boff, 16, 8 * SWQ, SWQ);
-          mma_f16_ss(s_tmem, adesc, bdesc, IDESC_S, kk > 0 ? 1u : 0u);
-        }
-        mma_commit(smem_u32(&sh.s_full[t][b]));
+      for (int kk = 0; kk < D / 16; ++kk) {
+        const uint32_t kbyte = static_cast<uint32_t>(kk) * 32u;
+        const uint32_t aoff = (kbyte / SWQ) * (128 * SWQ) + (kbyte % SWQ);
+        const uint32_t boff = (kbyte / SWQ) * (BN * SWQ) + (kbyte % SWQ);
+        const uint64_t adesc = make_smem_desc(q_smem + aoff, 16, 8 * SWQ, SWQ);
+        const uint64_t bdesc = make_smem_desc(ks + boff, 16, 8 * SWQ, SWQ);
+        mma_f16_ss(s_tmem, adesc, bdesc, IDESC_S, kk > 0 ? 1u : 0u);
       }
+      mma_commit(smem_u32(&sh.s_full[b]));
       mma_commit(smem_u32(&sh.k_empty[s]));
       if (j >= LAG && !pv_round(j - LAG)) {
         ok = false;
         break;
       }
     }
-    for (int i = max(0, nblk_max - LAG); i < nblk_max && ok; ++i) ok = pv_round(i);
+    for (int i = max(0, nblk - LAG); i < nblk && ok; ++i) ok = pv_round(i);
     if (!ok) {
       mma_commit(smem_u32(&sh.drain));
       mbar_wait_drain(smem_u32(&sh.drain), 0, err);
     }
   } else if (warp >= 4) {
     // ------------------------------------------- softmax / correction / epilogue
-    const int tile = (warp - 4) >> 2;  // query tile of this warpgroup
-    const int q = warp & 3;            // TMEM lane quarter of this warp
-    const int row = q * 32 + lane;     // query row within the tile == TMEM lane
-    const int tq0 = q0 + 128 * tile;
-    const int qrow = tq0 + row;
-    const int my_nblk = nblk_of(tile);
+    const int wg = (warp - 4) >> 2;  // warpgroup: which half of the columns
+    const int q = warp & 3;          // TMEM lane quarter of this warp
+    const int row = q * 32 + lane;   // query row within the tile == TMEM lane
+    const int qrow = q0 + row;
     const uint32_t lane_addr = static_cast<uint32_t>(q * 32) << 16;
-    const uint32_t o_tmem = tmem + static_cast<uint32_t>(tile * D);
+    const uint32_t o_tmem = tmem + lane_addr + static_cast<uint32_t>(wg * OC);
+    const int col0 = wg * SC;  // first S column of this warp
     const float2 scale2 = make_float2(scale_log2, scale_log2);
     float m_used = -INFINITY;
     float l = 0.f;
     bool ok = true;
-    for (int j = 0; j < my_nblk; ++j) {
+    // A failed (timed-out) wait clears ok; the loop then still runs to the
+    // end without touching TMEM so that both warps of a row pair meet at
+    // every named barrier (the other waits fail fast once abort is raised).
+    for (int j = 0; j < nblk; ++j) {
       const int b = j % NB;
       const uint32_t u = static_cast<uint32_t>(j / NB);
-      const uint32_t sp = tmem + lane_addr + static_cast<uint32_t>(NT * D + (tile * NB + b) * BN);
-      if (!mbar_wait(smem_u32(&sh.s_full[tile][b]), u & 1u, abort_flag, err, kErrWaitSoftmax)) {
+      const uint32_t sp = tmem + lane_addr + static_cast<uint32_t>(D + b * BN);
+      if (ok && !mbar_wait(smem_u32(&sh.s_full[b]), u & 1u, abort_flag, err, kErrWaitSoftmax))
         ok = false;
-        break;
-      }
+      ok = __all_sync(0xffffffffu, ok);  // warp-uniform from here on
       tc_fence_after();
-      // all BN/32 TMEM loads in flight before a single wait
-      float sv[BN];
-      {
-        uint32_t r[BN];
+      float sv[SC];
+      float mb = 0.f;
+      if (ok) {
+        // all TMEM loads of this warp's columns in flight before one wait
+        uint32_t r[SC];
 #pragma unroll
-        for (int c = 0; c < BN / 32; ++c)
-          tmem_ld32(sp + static_cast<uint32_t>(c * 32),
-                    *reinterpret_cast<uint32_t(*)[32]>(r + c * 32));
+        for (int c = 0; c < SC / SCH; ++c)
+          tmem_ld_cols<SCH>(sp + static_cast<uint32_t>(col0 + c * SCH), r + c * SCH);
         tmem_wait_ld();
 #pragma unroll
-        for (int i = 0; i < BN; ++i) sv[i] = __uint_as_float(r[i]);
-      }
-
-      // Mask padding / future keys only where the block needs it (block-
-      // uniform test on the tile's first row); work on raw scores, with the
-      // log2-domain scale folded into the exponent's FMA below.
-      const int key0 = j * BN;
-      const bool need_mask = key0 + BN > S || (CAUSAL && key0 + BN - 1 > tq0);
-      if (need_mask) {
+        for (int i = 0; i < SC; ++i) sv[i] = __uint_as_float(r[i]);
+        // Mask padding / future keys only where the block needs it (block-
+        // uniform test on the tile's first row); work on raw scores, with
+        // the log2-domain scale folded into the exponent's FMA below.
+        const int key0 = j * BN + col0;
+        const bool need_mask = j * BN + BN > S || (CAUSAL && j * BN + BN - 1 > q0);
+        if (need_mask) {
 #pragma unroll
-        for (int i = 0; i < BN; ++i) {
-          const int key = key0 + i;
-          if (key >= S || (CAUSAL && key > qrow)) sv[i] = -INFINITY;
+          for (int i = 0; i < SC; ++i) {
+            const int key = key0 + i;
+            if (key >= S || (CAUSAL && key > qrow)) sv[i] = -INFINITY;
+          }
         }
-      }
-      // row max: four independent three-input max chains
-      float mx[4] = {sv[0], sv[1], sv[2], sv[3]};
+        // row max: four independent three-input max chains
+        float mx[4] = {sv[0], sv[1], sv[2], sv[3]};
 #pragma unroll
-      for (int i = 4; i + 1 < BN; i += 2) mx[(i >> 1) & 3] = fmax3(mx[(i >> 1) & 3], sv[i], sv[i + 1]);
-      const float mb = fmaxf(fmax3(mx[0], mx[1], mx[2]), mx[3]) * scale_log2;
+        for (int i = 4; i + 1 < SC; i += 2)
+          mx[(i >> 1) & 3] = fmax3(mx[(i >> 1) & 3], sv[i], sv[i + 1]);
+        mb = fmaxf(fmax3(mx[0], mx[1], mx[2]), mx[3]) * scale_log2;
+      }
+      if constexpr (WG == 2) {
+        // combine with the other half of the row (warp pair q, q + 4); the
+        // barrier also orders both warps' S loads before either P store
+        xchg[((j & 1) * 2 + wg) * 128 + row] = mb;
+        tc_fence_before();
+        named_barrier(1 + q, 64);
+        tc_fence_after();
+        mb = fmaxf(mb, xchg[((j & 1) * 2 + (wg ^ 1)) * 128 + row]);
+      }
+      if (!ok) continue;
       if (j == 0) {
         m_used = mb;
       } else {
@@ -320,21 +340,22 @@ __global__ void __launch_bounds__(NT == 1 ? 256 : 384, 1)
           const float alpha = ex2_approx(m_used - m_new);
           // O holds PV_0..PV_{j-1}; wait for PV_{j-1} before rescaling it
           const int pj = j - 1;
-          if (!mbar_wait(smem_u32(&sh.pv_done[tile][pj % NB]),
-                         static_cast<uint32_t>(pj / NB) & 1u, abort_flag, err, kErrWaitSoftmax)) {
+          ok = mbar_wait(smem_u32(&sh.pv_done[pj % NB]), static_cast<uint32_t>(pj / NB) & 1u,
+                         abort_flag, err, kErrWaitSoftmax);
+          if (!__all_sync(0xffffffffu, ok)) {
             ok = false;
-            break;
+            continue;
           }
           tc_fence_after();
 #pragma unroll 1
-          for (int c = 0; c < D / 32; ++c) {
-            uint32_t r[32];
-            const uint32_t addr = o_tmem + lane_addr + static_cast<uint32_t>(c * 32);
-            tmem_ld32(addr, r);
+          for (int c = 0; c < OC / OCH; ++c) {
+            uint32_t r[OCH];
+            const uint32_t addr = o_tmem + static_cast<uint32_t>(c * OCH);
+            tmem_ld_cols<OCH>(addr, r);
             tmem_wait_ld();
 #pragma unroll
-            for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha);
-            tmem_st32(addr, r);
+            for (int i = 0; i < OCH; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha);
+            tmem_st_cols<OCH>(addr, r);
           }
           tmem_wait_st();
           l *= alpha;
@@ -347,9 +368,9 @@ __global__ void __launch_bounds__(NT == 1 ? 256 : 384, 1)
       const float2 shift2 = make_float2(neg_m, neg_m);
       float2 rs[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f),
                       make_float2(0.f, 0.f)};
-      uint32_t pk[BN / 2];
+      uint32_t pk[SC / 2];
 #pragma unroll
-      for (int g = 0; g < BN / 2; ++g) {
+      for (int g = 0; g < SC / 2; ++g) {
         const float2 x = __ffma2_rn(make_float2(sv[2 * g], sv[2 * g + 1]), scale2, shift2);
         const float2 p = make_float2(ex2_approx(x.x), ex2_approx(x.y));  // -inf -> 0
         rs[g & 3] = __fadd2_rn(rs[g & 3], p);
@@ -358,48 +379,52 @@ __global__ void __launch_bounds__(NT == 1 ? 256 : 384, 1)
       const float2 rs01 = __fadd2_rn(rs[0], rs[1]), rs23 = __fadd2_rn(rs[2], rs[3]);
       const float2 rsum = __fadd2_rn(rs01, rs23);
       l += rsum.x + rsum.y;
-      // P_j -> TMEM over the first BN/2 columns of its own S buffer (S_j
-      // has been read).  The MMA issuer writes S_{j+NB} into this buffer
-      // only after issuing PV_j, and tcgen05 MMAs execute in issue order.
-      if constexpr (BN / 2 >= 32) {
+      // P_j -> TMEM over the first BN/2 columns of its own S buffer (this
+      // warp: columns [col0/2, col0/2 + SC/2)).  The MMA issuer writes
+      // S_{j+NB} into this buffer only after issuing PV_j, and tcgen05 MMAs
+      // execute in issue order.
 #pragma unroll
-        for (int c = 0; c < BN / 64; ++c)
-          tmem_st32(sp + static_cast<uint32_t>(c * 32),
-                    *reinterpret_cast<const uint32_t(*)[32]>(pk + c * 32));
-      } else {
-        tmem_st16(sp, pk);
-      }
+      for (int c = 0; c < (SC / 2) / 16; ++c)
+        tmem_st16(sp + static_cast<uint32_t>(col0 / 2 + c * 16), pk + c * 16);
       tmem_wait_st();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(smem_u32(&sh.p_full[tile][b]));
+      if (lane == 0) mbar_arrive(smem_u32(&sh.p_full[b]));
     }
     // ------------------------------------------------------------ epilogue
-    if (ok && my_nblk > 0) {
-      const int pj = my_nblk - 1;
-      ok = mbar_wait(smem_u32(&sh.pv_done[tile][pj % NB]), static_cast<uint32_t>(pj / NB) & 1u,
+    if (ok && nblk > 0) {
+      const int pj = nblk - 1;
+      ok = mbar_wait(smem_u32(&sh.pv_done[pj % NB]), static_cast<uint32_t>(pj / NB) & 1u,
                      abort_flag, err, kErrWaitSoftmax);
+    }
+    ok = __all_sync(0xffffffffu, ok);
+    if constexpr (WG == 2) {
+      // full row sum from both halves (both warps of the pair reach this
+      // barrier whether or not their waits succeeded)
+      xchg[((nblk & 1) * 2 + wg) * 128 + row] = l;
+      named_barrier(1 + q, 64);
+      l += xchg[((nblk & 1) * 2 + (wg ^ 1)) * 128 + row];
     }
     if (ok) {
       tc_fence_after();
       const float inv_l = l > 0.f ? 1.0f / l : 0.f;
-      T* orow = O + (static_cast<int64_t>(bh) * S + qrow) * D;
+      T* orow = O + (static_cast<int64_t>(bh) * S + qrow) * D + wg * OC;
 #pragma unroll 1
-      for (int c = 0; c < D / 32; ++c) {
-        uint32_t r[32];
-        tmem_ld32(o_tmem + lane_addr + static_cast<uint32_t>(c * 32), r);
+      for (int c = 0; c < OC / OCH; ++c) {
+        uint32_t r[OCH];
+        tmem_ld_cols<OCH>(o_tmem + static_cast<uint32_t>(c * OCH), r);
         tmem_wait_ld();
         if (qrow < S) {
-          uint32_t pk[16];
+          uint32_t pk[OCH / 2];
 #pragma unroll
-          for (int i = 0; i < 16; ++i) {
+          for (int i = 0; i < OCH / 2; ++i) {
             const float lo = __uint_as_float(r[2 * i]) * inv_l;
             const float hi = __uint_as_float(r[2 * i + 1]) * inv_l;
             pk[i] = FMT == 1 ? pack_bf16(lo, hi) : pack_f16(lo, hi);
           }
-          uint4* d4 = reinterpret_cast<uint4*>(orow + c * 32);
+          uint4* d4 = reinterpret_cast<uint4*>(orow + c * OCH);
 #pragma unroll
-          for (int i = 0; i < 4; ++i)
+          for (int i = 0; i < OCH / 8; ++i)
             d4[i] = make_uint4(pk[4 * i], pk[4 * i + 1], pk[4 * i + 2], pk[4 * i + 3]);
         }
       }
@@ -435,56 +460,56 @@ static bool encode_bsd(CUtensorMap* map, CUtensorMapDataType dt, const void* ptr
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-static uint32_t attn_tc_smem(int BN, int D, int stages, int nt) {
+static uint32_t attn_tc_smem(int BN, int D, int stages) {
   auto al = [](uint32_t x) { return (x + 1023u) & ~1023u; };
   const uint32_t q = 128u * D * 2, kv = static_cast<uint32_t>(BN) * D * 2;
-  return static_cast<uint32_t>(nt) * al(q) + static_cast<uint32_t>(stages) * 2 * al(kv) + 1024u;
+  return al(q) + static_cast<uint32_t>(stages) * 2 * al(kv) + 1024u;
 }
 
-// Plan: aux[0] = dynamic smem bytes, aux[1] = query tiles per CTA (NT).
-// num_warps 4 -> one softmax warpgroup (NT = 1); 8 -> two (NT = 2).
+// Plan: aux[0] = dynamic smem bytes, aux[1] = softmax warpgroups (WG).
+// num_warps 4 -> one softmax warpgroup; 8 -> two splitting each row's
+// columns (BLOCK_N >= 64; with BLOCK_N 32 a warp would hold fewer than the
+// 32 columns of one TMEM access, so the kernel keeps one warpgroup).
 gpo_status plan_attention_tc(const gpo_key& k, Plan& p, std::string& log) {
   const int D = static_cast<int>(k.shape[2]);
   const int BN = k.block_n;
-  const int nt = k.num_warps == 8 ? 2 : 1;
+  const int wg = (k.num_warps == 8 && BN >= 64) ? 2 : 1;
   if (k.num_stages < 1 || k.num_stages > kAttnMaxStages) {
     log = "num_stages must be in [1, 4]";
     return GPO_BAD_CONFIG;
   }
-  const int min_cols = nt * (D + 2 * BN);
+  const int min_cols = D + 2 * BN;
   if (min_cols > static_cast<int>(kTmemCols)) {
-    log = "TMEM needs " + std::to_string(min_cols) + " columns (" + std::to_string(nt) +
-          " query tiles x (O " + std::to_string(D) + " + 2 S buffers x " + std::to_string(BN) +
-          ")) > 512";
+    log = "TMEM needs " + std::to_string(min_cols) + " columns (O " + std::to_string(D) +
+          " + 2 S buffers x " + std::to_string(BN) + ") > 512";
     return GPO_COMPILE_ERROR;
   }
-  const int cols_needed = nt * (D + attn_sbufs(nt, D, BN) * BN);
-  const uint32_t dyn = attn_tc_smem(BN, D, k.num_stages, nt);
+  const int cols_needed = D + attn_sbufs(D, BN) * BN;
+  const uint32_t dyn = attn_tc_smem(BN, D, k.num_stages) + (wg == 2 ? kAttnXchgBytes : 0u);
   const uint32_t smem = dyn + static_cast<uint32_t>(sizeof(AttnShared));
   if (smem > kMaxSmemPerCta) {
-    log = "shared memory " + std::to_string(smem) + " B (" + std::to_string(nt) +
-          " Q tiles, " + std::to_string(k.num_stages) +
-          " K/V stages) exceeds the 232448 B per-CTA limit";
+    log = "shared memory " + std::to_string(smem) + " B (Q tile + " +
+          std::to_string(k.num_stages) + " K and V stages) exceeds the 232448 B per-CTA limit";
     return GPO_COMPILE_ERROR;
   }
   p.aux[0] = static_cast<int>(dyn);
-  p.aux[1] = nt;
+  p.aux[1] = wg;
   p.family = "attn_tc";
   p.res.smem_bytes = smem;
   p.res.tmem_cols = static_cast<uint32_t>(attn_tmem_alloc(cols_needed));
-  p.res.threads_per_cta = nt == 2 ? 384u : 256u;
-  p.res.grid_x = static_cast<uint32_t>(cdiv(k.shape[1], 128 * nt));
+  p.res.threads_per_cta = static_cast<uint32_t>(128 + 128 * wg);
+  p.res.grid_x = static_cast<uint32_t>(cdiv(k.shape[1], 128));
   p.res.grid_y = static_cast<uint32_t>(k.shape[0]);
   p.res.grid_z = 1;
   p.res.launches_per_call = 1;
-  snprintf(p.res.kernel, sizeof(p.res.kernel), "attn_tc_kernel<%s,BN=%d,D=%d,%s,tiles=%d,sbufs=%d>",
+  snprintf(p.res.kernel, sizeof(p.res.kernel), "attn_tc_kernel<%s,BN=%d,D=%d,%s,wg=%d,sbufs=%d>",
            k.dtype == GPO_BFLOAT16 ? "bf16" : "f16", BN, D,
-           k.task == GPO_TASK_ATTENTION_CAUSAL ? "causal" : "full", nt, attn_sbufs(nt, D, BN));
+           k.task == GPO_TASK_ATTENTION_CAUSAL ? "causal" : "full", wg, attn_sbufs(D, BN));
   return GPO_OK;
 }
 
-template <typename T, int FMT, int BN, int D, bool CAUSAL, int NT>
-static gpo_status run_attn_tc_nt(const gpo_key& k, const Plan& p, const gpo_args& a,
+template <typename T, int FMT, int BN, int D, bool CAUSAL, int WG>
+static gpo_status run_attn_tc_wg(const gpo_key& k, const Plan& p, const gpo_args& a,
                                  const LaunchCtx& c, CUtensorMapDataType dt) {
   const uint64_t BH = static_cast<uint64_t>(k.shape[0]), S = static_cast<uint64_t>(k.shape[1]);
   constexpr int SW = (D * 2) < 128 ? (D * 2) : 128;
@@ -493,26 +518,30 @@ static gpo_status run_attn_tc_nt(const gpo_key& k, const Plan& p, const gpo_args
       !encode_bsd(&mk, dt, a.in[1], BH, S, D, BN, SW) ||
       !encode_bsd(&mv, dt, a.in[2], BH, S, D, BN, SW))
     return GPO_LAUNCH_ERROR;
-  auto kern = attn_tc_kernel<T, FMT, BN, D, CAUSAL, NT>;
+  auto kern = attn_tc_kernel<T, FMT, BN, D, CAUSAL, WG>;
   const uint32_t dyn = static_cast<uint32_t>(p.aux[0]);
   gpo_status s = ensure_smem_attr(reinterpret_cast<const void*>(kern), dyn);
   if (s != GPO_OK) return s;
-  const dim3 grid(static_cast<unsigned>(cdiv(S, 128 * NT)), static_cast<unsigned>(BH));
+  const dim3 grid(static_cast<unsigned>(cdiv(S, 128)), static_cast<unsigned>(BH));
   const float scale_log2 = 1.4426950408889634f / sqrtf(static_cast<float>(D));
-  kern<<<grid, NT == 2 ? 384 : 256, dyn, c.stream>>>(mq, mk, mv, static_cast<T*>(a.out),
-                                                     static_cast<int>(S), k.num_stages,
-                                                     scale_log2, c.err);
+  kern<<<grid, 128 + 128 * WG, dyn, c.stream>>>(mq, mk, mv, static_cast<T*>(a.out),
+                                                 static_cast<int>(S), k.num_stages, scale_log2,
+                                                 c.err);
   return launch_status();
 }
 
 template <typename T, int FMT, int BN, int D, bool CAUSAL>
 static gpo_status run_attn_tc(const gpo_key& k, const Plan& p, const gpo_args& a,
                               const LaunchCtx& c, CUtensorMapDataType dt) {
-  if constexpr (2 * (D + 2 * BN) <= 512) {
-    if (p.aux[1] == 2) return run_attn_tc_nt<T, FMT, BN, D, CAUSAL, 2>(k, p, a, c, dt);
+  if constexpr (D + 2 * BN <= 512) {
+    if constexpr (BN >= 64) {
+      if (p.aux[1] == 2) return run_attn_tc_wg<T, FMT, BN, D, CAUSAL, 2>(k, p, a, c, dt);
+    }
+    if (p.aux[1] != 1) return GPO_INTERNAL;
+    return run_attn_tc_wg<T, FMT, BN, D, CAUSAL, 1>(k, p, a, c, dt);
+  } else {
+    return GPO_INTERNAL;  // rejected by the plan (TMEM)
   }
-  if (p.aux[1] != 1) return GPO_INTERNAL;
-  return run_attn_tc_nt<T, FMT, BN, D, CAUSAL, 1>(k, p, a, c, dt);
 }
 
 template <typename T, int FMT, int BN, bool CAUSAL>

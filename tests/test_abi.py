@@ -74,15 +74,20 @@ def test_attention_plans():
     base = {"BLOCK_M": 128, "BLOCK_N": 128, "num_warps": 4, "num_stages": 2,
             "dtype": "bfloat16"}
     r = compile_module("attention_causal", (128, 4096, 128), base).resources()
-    assert r["kernel"] == "attn_tc_kernel<bf16,BN=128,D=128,causal,tiles=1,sbufs=3>"
+    assert r["kernel"] == "attn_tc_kernel<bf16,BN=128,D=128,causal,wg=1,sbufs=3>"
     assert r["tmem_cols"] == 512 and r["grid"] == [32, 128, 1]
+    # 8 warps: two softmax warpgroups split each row's columns
     r2 = compile_module("attention_causal", (128, 4096, 128),
-                        {**base, "BLOCK_N": 64, "num_warps": 8}).resources()
-    assert r2["kernel"].endswith("tiles=2,sbufs=2>") and r2["threads_per_cta"] == 384
-    assert r2["grid"] == [16, 128, 1] and r2["tmem_cols"] == 512
-    with pytest.raises(KernelBuildError) as ei:  # 2 x (O 128 + 2 x S 128) columns
-        compile_module("attention_causal", (128, 4096, 128), {**base, "num_warps": 8})
-    assert "TMEM" in str(ei.value)
+                        {**base, "num_warps": 8}).resources()
+    assert r2["kernel"].endswith("wg=2,sbufs=3>") and r2["threads_per_cta"] == 384
+    assert r2["grid"] == [32, 128, 1] and r2["tmem_cols"] == 512
+    # BLOCK_N 32 keeps one warpgroup (a warp needs 32 S columns)
+    r3 = compile_module("attention", (16, 1024, 64),
+                        {**base, "BLOCK_N": 32, "num_warps": 8}).resources()
+    assert r3["kernel"].endswith("wg=1,sbufs=3>") and r3["threads_per_cta"] == 256
+    # D = 256 with BLOCK_N 128: O 256 + 2 S buffers x 128 fill TMEM (two buffers)
+    r4 = compile_module("attention", (4, 512, 256), {**base, "num_stages": 1}).resources()
+    assert r4["kernel"].endswith("sbufs=2>") and r4["tmem_cols"] == 512
     # Q (32 KB) + 3 K/V stages of 64 KB fit (P lives in TMEM); 4 do not
     compile_module("attention_causal", (128, 4096, 128), {**base, "num_stages": 3})
     with pytest.raises(KernelBuildError):
