@@ -100,7 +100,7 @@ __device__ __forceinline__ void tmem_st_cols(uint32_t taddr, const uint32_t* r) 
     tmem_st16(taddr, r);
 }
 
-template <typename T, int FMT, int BN, int D, bool CAUSAL, int WG>
+template <typename T, int FMT, int BN, int D, bool CAUSAL, int WG, bool PAIR>
 __global__ void __launch_bounds__(128 + 128 * WG, 1)
     attn_tc_kernel(const __grid_constant__ CUtensorMap tma_q,
                    const __grid_constant__ CUtensorMap tma_k,
@@ -109,14 +109,19 @@ __global__ void __launch_bounds__(128 + 128 * WG, 1)
   constexpr int ES = 2;
   constexpr int SWQ = (D * ES) < 128 ? (D * ES) : 128;  // swizzle of Q/K/V rows
   constexpr uint32_t Q_BYTES = 128u * D * ES;
-  constexpr uint32_t KV_BYTES = static_cast<uint32_t>(BN) * D * ES;
+  // PAIR: each CTA stages half of K's rows and half of V's columns
+  constexpr int KROWS = PAIR ? BN / 2 : BN;     // K rows per CTA
+  constexpr int VCOLS = PAIR ? D / 2 : D;       // V columns per CTA
+  constexpr int SWV = (VCOLS * ES) < 128 ? (VCOLS * ES) : 128;  // swizzle of V rows
+  constexpr uint32_t KV_BYTES = static_cast<uint32_t>(KROWS) * D * ES;  // = BN * VCOLS * ES
   constexpr uint32_t KV_SLOT = (KV_BYTES + 1023u) & ~1023u;
   constexpr int NB = attn_sbufs(D, BN);
   constexpr int LAG = NB - 1;  // S MMAs run LAG blocks ahead of PV MMAs
   constexpr int COLS = D + NB * BN;
   constexpr int ALLOC = attn_tmem_alloc(COLS);
-  constexpr uint32_t IDESC_S = make_idesc(FMT, 128, BN, false, false);
-  constexpr uint32_t IDESC_O = make_idesc(FMT, 128, D, false, true);
+  constexpr int MMA_M = PAIR ? 256 : 128;
+  constexpr uint32_t IDESC_S = make_idesc(FMT, MMA_M, BN, false, false);
+  constexpr uint32_t IDESC_O = make_idesc(FMT, MMA_M, D, false, true);
   constexpr int SC = BN / WG;        // S columns per softmax warp
   constexpr int OC = D / WG;         // O columns per softmax warp
   constexpr int SCH = SC < 32 ? SC : 32;  // TMEM access chunk (S)
@@ -134,13 +139,18 @@ __global__ void __launch_bounds__(128 + 128 * WG, 1)
       dyn_smem + (v_smem + static_cast<uint32_t>(stages) * KV_SLOT - smem_u32(dyn_smem)));
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int num_q_tiles = (S + 127) / 128;
+  // PAIR: cluster c holds query tiles 2c (even CTA) and 2c + 1 (odd CTA)
+  const uint32_t rank = PAIR ? cluster_ctarank() : 0u;
+  const int units = PAIR ? (S + 255) / 256 : (S + 127) / 128;  // tiles or tile pairs
+  const int unit = static_cast<int>(PAIR ? (blockIdx.x >> 1) : blockIdx.x);
   // longest causal rows first; identity order for the non-causal task
-  const int qt = CAUSAL ? (num_q_tiles - 1 - static_cast<int>(blockIdx.x))
-                        : static_cast<int>(blockIdx.x);
-  const int q0 = qt * 128;
+  const int ut = CAUSAL ? (units - 1 - unit) : unit;
+  const int q0 = PAIR ? (2 * ut + static_cast<int>(rank)) * 128 : ut * 128;
   const int bh = blockIdx.y;
-  const int nblk = ((CAUSAL ? min(S, q0 + 128) : S) + BN - 1) / BN;  // causal: stop at diagonal
+  // K/V blocks the MMAs run over (causal: up to the diagonal of the unit's
+  // last tile; the even CTA of a pair masks its extra blocks to P = 0)
+  const int kv_len = CAUSAL ? min(S, (PAIR ? 2 * ut + 2 : ut + 1) * 128) : S;
+  const int nblk = (kv_len + BN - 1) / BN;
 
   if (threadIdx.x == 0) {
     mbar_init(smem_u32(&sh.q_full), 1);
@@ -152,7 +162,7 @@ __global__ void __launch_bounds__(128 + 128 * WG, 1)
     }
     for (int b = 0; b < NB; ++b) {
       mbar_init(smem_u32(&sh.s_full[b]), 1);
-      mbar_init(smem_u32(&sh.p_full[b]), 4 * WG);
+      mbar_init(smem_u32(&sh.p_full[b]), 4 * WG * (PAIR ? 2 : 1));  // PAIR: both CTAs' warps
       mbar_init(smem_u32(&sh.pv_done[b]), 1);
     }
     mbar_init(smem_u32(&sh.drain), 1);
@@ -163,11 +173,19 @@ __global__ void __launch_bounds__(128 + 128 * WG, 1)
     tma_prefetch_desc(&tma_v);
   }
   if (warp == 2) {
-    tmem_alloc(smem_u32(&sh.tmem_base), ALLOC);
-    tmem_relinquish();
+    if constexpr (PAIR) {
+      tmem_alloc_pair(smem_u32(&sh.tmem_base), ALLOC);
+      tmem_relinquish_pair();
+    } else {
+      tmem_alloc(smem_u32(&sh.tmem_base), ALLOC);
+      tmem_relinquish();
+    }
   }
   tc_fence_before();
-  __syncthreads();
+  if constexpr (PAIR)
+    cluster_sync_all();  // both CTAs' barriers initialised before any remote signal
+  else
+    __syncthreads();
   tc_fence_after();
   const uint32_t tmem = sh.tmem_base;
   volatile int* abort_flag = &sh.abort;
@@ -181,12 +199,22 @@ __global__ void __launch_bounds__(128 + 128 * WG, 1)
     uint64_t* empty = is_k ? sh.k_empty : sh.v_empty;
     bool ok = true;
     int issued = 0;
+    // PAIR: the even CTA's full barriers count both CTAs' bytes (pair loads)
+    const uint32_t mult = PAIR ? 2u : 1u;
+    auto lead = [&](const uint64_t* bar) -> uint32_t {
+      return PAIR ? mapa_shared(smem_u32(bar), 0) : smem_u32(bar);
+    };
+    auto load = [&](uint32_t dst, const CUtensorMap* m, uint32_t bar, int x, int y) {
+      if constexpr (PAIR)
+        tma_load_3d_pair(dst, m, bar, x, y, bh);
+      else
+        tma_load_3d(dst, m, bar, x, y, bh);
+    };
     if (is_k) {
-      mbar_arrive_expect_tx(smem_u32(&sh.q_full), Q_BYTES);
+      if (rank == 0) mbar_arrive_expect_tx(smem_u32(&sh.q_full), mult * Q_BYTES);
 #pragma unroll
       for (int a = 0; a < (D * ES) / SWQ; ++a)
-        tma_load_3d(q_smem + a * 128 * SWQ, &tma_q, smem_u32(&sh.q_full), a * (SWQ / ES), q0,
-                    bh);
+        load(q_smem + a * 128 * SWQ, &tma_q, lead(&sh.q_full), a * (SWQ / ES), q0);
     }
     for (int j = 0; j < nblk; ++j) {
       const int s = j % stages;
@@ -195,22 +223,47 @@ __global__ void __launch_bounds__(128 + 128 * WG, 1)
         ok = false;
         break;
       }
-      const uint32_t fb = smem_u32(&full[s]);
+      const uint32_t fb = lead(&full[s]);
       const uint32_t dst = ring + static_cast<uint32_t>(s) * KV_SLOT;
-      mbar_arrive_expect_tx(fb, KV_BYTES);
+      if (rank == 0) mbar_arrive_expect_tx(smem_u32(&full[s]), mult * KV_BYTES);
+      if (is_k) {
+        // K rows [j*BN + rank*KROWS, +KROWS), all D columns (K-major atoms)
 #pragma unroll
-      for (int a = 0; a < (D * ES) / SWQ; ++a)
-        tma_load_3d(dst + a * BN * SWQ, map, fb, a * (SWQ / ES), j * BN, bh);
+        for (int a = 0; a < (D * ES) / SWQ; ++a)
+          load(dst + a * KROWS * SWQ, map, fb, a * (SWQ / ES), j * BN + static_cast<int>(rank) * KROWS);
+      } else {
+        // V rows [j*BN, +BN), columns [rank*VCOLS, +VCOLS) (MN-major chunks)
+#pragma unroll
+        for (int a = 0; a < (VCOLS * ES) / SWV; ++a)
+          load(dst + a * BN * SWV, map, fb, static_cast<int>(rank) * VCOLS + a * (SWV / ES), j * BN);
+      }
       issued = j + 1;
     }
     if (!ok) {
-      if (is_k) mbar_wait_drain(smem_u32(&sh.q_full), 0, err);
-      for (int j = max(0, issued - stages); j < issued; ++j)
-        mbar_wait_drain(smem_u32(&full[j % stages]), static_cast<uint32_t>(j / stages) & 1u, err);
+      if (rank == 0) {
+        if (is_k) mbar_wait_drain(smem_u32(&sh.q_full), 0, err);
+        for (int j = max(0, issued - stages); j < issued; ++j)
+          mbar_wait_drain(smem_u32(&full[j % stages]), static_cast<uint32_t>(j / stages) & 1u,
+                          err);
+      } else {
+        // the odd CTA's loads complete on the even CTA's barriers, which it
+        // cannot poll: give in-flight copies time to land before exiting
+        const unsigned long long t0 = globaltimer_ns();
+        while (globaltimer_ns() - t0 < 200000ull) __nanosleep(1000);
+      }
     }
-  } else if (warp == 1 && lane == 0) {
-    // ---------------------------------------------------------- MMA issuer
+  } else if (warp == 1 && lane == 0 && rank == 0) {
+    // ----------------------------------------------- MMA issuer (even CTA)
     bool ok = mbar_wait(smem_u32(&sh.q_full), 0, abort_flag, err, kErrWaitMma);
+    // commits reach this CTA's barrier and, for a pair, the odd CTA's twin
+    auto commit2 = [&](const uint64_t* bar) {
+      if constexpr (PAIR) {
+        mma_commit_pair(smem_u32(bar));
+        mma_commit_pair(mapa_shared(smem_u32(bar), 1));
+      } else {
+        mma_commit(smem_u32(bar));
+      }
+    };
     // O += P(i) V(i), then release V slot i.
     auto pv_round = [&](int i) -> bool {
       const int s = i % stages;
@@ -218,19 +271,23 @@ __global__ void __launch_bounds__(128 + 128 * WG, 1)
       const int b = i % NB;
       const uint32_t u = static_cast<uint32_t>(i / NB);
       if (!mbar_wait(smem_u32(&sh.v_full[s]), r & 1u, abort_flag, err, kErrWaitMma)) return false;
-      if (!mbar_wait(smem_u32(&sh.p_full[b]), u & 1u, abort_flag, err, kErrWaitMma)) return false;
+      if (!mbar_wait<PAIR>(smem_u32(&sh.p_full[b]), u & 1u, abort_flag, err, kErrWaitMma))
+        return false;
       tc_fence_after();
       const uint32_t vs = v_smem + static_cast<uint32_t>(s) * KV_SLOT;
       // P(i) sits in the first BN/2 columns of S/P buffer b (16-bit pairs)
       const uint32_t pa = tmem + static_cast<uint32_t>(D + b * BN);
 #pragma unroll
       for (int kk = 0; kk < BN / 16; ++kk) {
-        const uint64_t bdesc = make_smem_desc(vs + kk * 16 * SWQ, BN * SWQ, 8 * SWQ, SWQ);
-        mma_f16_ts(tmem, pa + static_cast<uint32_t>(kk * 8), bdesc, IDESC_O,
-                   (i > 0 || kk > 0) ? 1u : 0u);
+        const uint64_t bdesc = make_smem_desc(vs + kk * 16 * SWV, BN * SWV, 8 * SWV, SWV);
+        const uint32_t acc = (i > 0 || kk > 0) ? 1u : 0u;
+        if constexpr (PAIR)
+          mma_f16_ts_pair(tmem, pa + static_cast<uint32_t>(kk * 8), bdesc, IDESC_O, acc);
+        else
+          mma_f16_ts(tmem, pa + static_cast<uint32_t>(kk * 8), bdesc, IDESC_O, acc);
       }
-      mma_commit(smem_u32(&sh.pv_done[b]));
-      mma_commit(smem_u32(&sh.v_empty[s]));
+      commit2(&sh.pv_done[b]);
+      commit2(&sh.v_empty[s]);
       return true;
     };
     for (int j = 0; j < nblk && ok; ++j) {
@@ -250,13 +307,16 @@ __global__ void __launch_bounds__(128 + 128 * WG, 1)
       for (int kk = 0; kk < D / 16; ++kk) {
         const uint32_t kbyte = static_cast<uint32_t>(kk) * 32u;
         const uint32_t aoff = (kbyte / SWQ) * (128 * SWQ) + (kbyte % SWQ);
-        const uint32_t boff = (kbyte / SWQ) * (BN * SWQ) + (kbyte % SWQ);
+        const uint32_t boff = (kbyte / SWQ) * (KROWS * SWQ) + (kbyte % SWQ);
         const uint64_t adesc = make_smem_desc(q_smem + aoff, 16, 8 * SWQ, SWQ);
         const uint64_t bdesc = make_smem_desc(ks + boff, 16, 8 * SWQ, SWQ);
-        mma_f16_ss(s_tmem, adesc, bdesc, IDESC_S, kk > 0 ? 1u : 0u);
+        if constexpr (PAIR)
+          mma_f16_ss_pair(s_tmem, adesc, bdesc, IDESC_S, kk > 0 ? 1u : 0u);
+        else
+          mma_f16_ss(s_tmem, adesc, bdesc, IDESC_S, kk > 0 ? 1u : 0u);
       }
-      mma_commit(smem_u32(&sh.s_full[b]));
-      mma_commit(smem_u32(&sh.k_empty[s]));
+      commit2(&sh.s_full[b]);
+      commit2(&sh.k_empty[s]);
       if (j >= LAG && !pv_round(j - LAG)) {
         ok = false;
         break;
@@ -264,7 +324,10 @@ __global__ void __launch_bounds__(128 + 128 * WG, 1)
     }
     for (int i = max(0, nblk - LAG); i < nblk && ok; ++i) ok = pv_round(i);
     if (!ok) {
-      mma_commit(smem_u32(&sh.drain));
+      if constexpr (PAIR)
+        mma_commit_pair(smem_u32(&sh.drain));
+      else
+        mma_commit(smem_u32(&sh.drain));
       mbar_wait_drain(smem_u32(&sh.drain), 0, err);
     }
   } else if (warp >= 4) {
@@ -389,7 +452,12 @@ __global__ void __launch_bounds__(128 + 128 * WG, 1)
       tmem_wait_st();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(smem_u32(&sh.p_full[b]));
+      if (lane == 0) {
+        if constexpr (PAIR)
+          mbar_arrive_cluster(mapa_shared(smem_u32(&sh.p_full[b]), 0));  // even CTA's barrier
+        else
+          mbar_arrive(smem_u32(&sh.p_full[b]));
+      }
     }
     // ------------------------------------------------------------ epilogue
     if (ok && nblk > 0) {
@@ -433,8 +501,14 @@ __global__ void __launch_bounds__(128 + 128 * WG, 1)
 
   tc_fence_before();
   __syncthreads();
+  if constexpr (PAIR) cluster_sync_all();  // no CTA leaves while its peer may still signal it
   tc_fence_after();
-  if (warp == 2) tmem_dealloc(tmem, ALLOC);
+  if (warp == 2) {
+    if constexpr (PAIR)
+      tmem_dealloc_pair(tmem, ALLOC);
+    else
+      tmem_dealloc(tmem, ALLOC);
+  }
 }
 
 // ------------------------------------------------------------------- host
@@ -460,13 +534,19 @@ static bool encode_bsd(CUtensorMap* map, CUtensorMapDataType dt, const void* ptr
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-static uint32_t attn_tc_smem(int BN, int D, int stages) {
+static uint32_t attn_tc_smem(int BN, int D, int stages, bool pair) {
   auto al = [](uint32_t x) { return (x + 1023u) & ~1023u; };
-  const uint32_t q = 128u * D * 2, kv = static_cast<uint32_t>(BN) * D * 2;
+  const uint32_t q = 128u * D * 2;
+  const uint32_t kv = static_cast<uint32_t>(pair ? BN / 2 : BN) * D * 2;  // a K (or V) slot
   return al(q) + static_cast<uint32_t>(stages) * 2 * al(kv) + 1024u;
 }
 
-// Plan: aux[0] = dynamic smem bytes, aux[1] = softmax warpgroups (WG).
+// Plan: aux[0] = dynamic smem bytes, aux[1] = softmax warpgroups (WG),
+// aux[2] = CTA pair.
+// BLOCK_M 128 -> one 128-row query tile per CTA; 256 -> a cluster of two
+// CTAs on two consecutive query tiles of a head, sharing each K/V block
+// through M=256 cta_group::2 MMAs (each CTA stages half of K's rows and half
+// of V's columns, halving the shared-memory and TMA bytes per tile).
 // num_warps 4 -> one softmax warpgroup; 8 -> two splitting each row's
 // columns (BLOCK_N >= 64; with BLOCK_N 32 a warp would hold fewer than the
 // 32 columns of one TMEM access, so the kernel keeps one warpgroup).
@@ -474,6 +554,7 @@ gpo_status plan_attention_tc(const gpo_key& k, Plan& p, std::string& log) {
   const int D = static_cast<int>(k.shape[2]);
   const int BN = k.block_n;
   const int wg = (k.num_warps == 8 && BN >= 64) ? 2 : 1;
+  const bool pair = k.block_m == 256;
   if (k.num_stages < 1 || k.num_stages > kAttnMaxStages) {
     log = "num_stages must be in [1, 4]";
     return GPO_BAD_CONFIG;
@@ -485,7 +566,8 @@ gpo_status plan_attention_tc(const gpo_key& k, Plan& p, std::string& log) {
     return GPO_COMPILE_ERROR;
   }
   const int cols_needed = D + attn_sbufs(D, BN) * BN;
-  const uint32_t dyn = attn_tc_smem(BN, D, k.num_stages) + (wg == 2 ? kAttnXchgBytes : 0u);
+  const uint32_t dyn =
+      attn_tc_smem(BN, D, k.num_stages, pair) + (wg == 2 ? kAttnXchgBytes : 0u);
   const uint32_t smem = dyn + static_cast<uint32_t>(sizeof(AttnShared));
   if (smem > kMaxSmemPerCta) {
     log = "shared memory " + std::to_string(smem) + " B (Q tile + " +
@@ -494,39 +576,62 @@ gpo_status plan_attention_tc(const gpo_key& k, Plan& p, std::string& log) {
   }
   p.aux[0] = static_cast<int>(dyn);
   p.aux[1] = wg;
+  p.aux[2] = pair ? 1 : 0;
   p.family = "attn_tc";
   p.res.smem_bytes = smem;
   p.res.tmem_cols = static_cast<uint32_t>(attn_tmem_alloc(cols_needed));
   p.res.threads_per_cta = static_cast<uint32_t>(128 + 128 * wg);
-  p.res.grid_x = static_cast<uint32_t>(cdiv(k.shape[1], 128));
+  p.res.grid_x = static_cast<uint32_t>(pair ? 2 * cdiv(k.shape[1], 256) : cdiv(k.shape[1], 128));
   p.res.grid_y = static_cast<uint32_t>(k.shape[0]);
   p.res.grid_z = 1;
   p.res.launches_per_call = 1;
-  snprintf(p.res.kernel, sizeof(p.res.kernel), "attn_tc_kernel<%s,BN=%d,D=%d,%s,wg=%d,sbufs=%d>",
+  snprintf(p.res.kernel, sizeof(p.res.kernel), "attn_tc_kernel<%s,BN=%d,D=%d,%s,wg=%d,sbufs=%d%s>",
            k.dtype == GPO_BFLOAT16 ? "bf16" : "f16", BN, D,
-           k.task == GPO_TASK_ATTENTION_CAUSAL ? "causal" : "full", wg, attn_sbufs(D, BN));
+           k.task == GPO_TASK_ATTENTION_CAUSAL ? "causal" : "full", wg, attn_sbufs(D, BN),
+           pair ? ",cta_pair" : "");
   return GPO_OK;
 }
 
-template <typename T, int FMT, int BN, int D, bool CAUSAL, int WG>
+template <typename T, int FMT, int BN, int D, bool CAUSAL, int WG, bool PAIR>
 static gpo_status run_attn_tc_wg(const gpo_key& k, const Plan& p, const gpo_args& a,
                                  const LaunchCtx& c, CUtensorMapDataType dt) {
   const uint64_t BH = static_cast<uint64_t>(k.shape[0]), S = static_cast<uint64_t>(k.shape[1]);
   constexpr int SW = (D * 2) < 128 ? (D * 2) : 128;
+  constexpr int SWV = (PAIR ? D : D * 2) < 128 ? (PAIR ? D : D * 2) : 128;  // V half: D/2 columns
   CUtensorMap mq, mk, mv;
   if (!encode_bsd(&mq, dt, a.in[0], BH, S, D, 128, SW) ||
-      !encode_bsd(&mk, dt, a.in[1], BH, S, D, BN, SW) ||
-      !encode_bsd(&mv, dt, a.in[2], BH, S, D, BN, SW))
+      !encode_bsd(&mk, dt, a.in[1], BH, S, D, PAIR ? BN / 2 : BN, SW) ||
+      !encode_bsd(&mv, dt, a.in[2], BH, S, D, BN, SWV))
     return GPO_LAUNCH_ERROR;
-  auto kern = attn_tc_kernel<T, FMT, BN, D, CAUSAL, WG>;
+  auto kern = attn_tc_kernel<T, FMT, BN, D, CAUSAL, WG, PAIR>;
   const uint32_t dyn = static_cast<uint32_t>(p.aux[0]);
   gpo_status s = ensure_smem_attr(reinterpret_cast<const void*>(kern), dyn);
   if (s != GPO_OK) return s;
-  const dim3 grid(static_cast<unsigned>(cdiv(S, 128)), static_cast<unsigned>(BH));
+  const dim3 grid(static_cast<unsigned>(PAIR ? 2 * cdiv(S, 256) : cdiv(S, 128)),
+                  static_cast<unsigned>(BH));
   const float scale_log2 = 1.4426950408889634f / sqrtf(static_cast<float>(D));
-  kern<<<grid, 128 + 128 * WG, dyn, c.stream>>>(mq, mk, mv, static_cast<T*>(a.out),
-                                                 static_cast<int>(S), k.num_stages, scale_log2,
-                                                 c.err);
+  T* out = static_cast<T*>(a.out);
+  const int Si = static_cast<int>(S), stages = k.num_stages;
+  if constexpr (PAIR) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = dim3(128 + 128 * WG, 1, 1);
+    cfg.dynamicSmemBytes = dyn;
+    cfg.stream = c.stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    if (cudaLaunchKernelEx(&cfg, kern, mq, mk, mv, out, Si, stages, scale_log2, c.err) !=
+        cudaSuccess)
+      return launch_status();
+  } else {
+    kern<<<grid, 128 + 128 * WG, dyn, c.stream>>>(mq, mk, mv, out, Si, stages, scale_log2,
+                                                   c.err);
+  }
   return launch_status();
 }
 
@@ -534,11 +639,15 @@ template <typename T, int FMT, int BN, int D, bool CAUSAL>
 static gpo_status run_attn_tc(const gpo_key& k, const Plan& p, const gpo_args& a,
                               const LaunchCtx& c, CUtensorMapDataType dt) {
   if constexpr (D + 2 * BN <= 512) {
+    const bool pair = p.aux[2] != 0;
     if constexpr (BN >= 64) {
-      if (p.aux[1] == 2) return run_attn_tc_wg<T, FMT, BN, D, CAUSAL, 2>(k, p, a, c, dt);
+      if (p.aux[1] == 2)
+        return pair ? run_attn_tc_wg<T, FMT, BN, D, CAUSAL, 2, true>(k, p, a, c, dt)
+                    : run_attn_tc_wg<T, FMT, BN, D, CAUSAL, 2, false>(k, p, a, c, dt);
     }
     if (p.aux[1] != 1) return GPO_INTERNAL;
-    return run_attn_tc_wg<T, FMT, BN, D, CAUSAL, 1>(k, p, a, c, dt);
+    return pair ? run_attn_tc_wg<T, FMT, BN, D, CAUSAL, 1, true>(k, p, a, c, dt)
+                : run_attn_tc_wg<T, FMT, BN, D, CAUSAL, 1, false>(k, p, a, c, dt);
   } else {
     return GPO_INTERNAL;  // rejected by the plan (TMEM)
   }

@@ -503,7 +503,7 @@ class AttentionTask(Task):
 
     def param_space(self, shape):
         if self.profile == "b200":
-            specs = [ParamSpec("BLOCK_M", (64, 128)), ParamSpec("BLOCK_N", (32, 64, 128)),
+            specs = [ParamSpec("BLOCK_M", (64, 128, 256)), ParamSpec("BLOCK_N", (32, 64, 128)),
                      ParamSpec("num_warps", (4, 8)), ParamSpec("num_stages", (2, 3, 4)),
                      ParamSpec("dtype", ("float16", "bfloat16"))]
         else:

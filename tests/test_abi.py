@@ -85,6 +85,11 @@ def test_attention_plans():
     r3 = compile_module("attention", (16, 1024, 64),
                         {**base, "BLOCK_N": 32, "num_warps": 8}).resources()
     assert r3["kernel"].endswith("wg=1,sbufs=3>") and r3["threads_per_cta"] == 256
+    # BLOCK_M 256: a CTA pair per two query tiles
+    r5 = compile_module("attention_causal", (128, 4096, 128),
+                        {**base, "BLOCK_M": 256, "num_stages": 4}).resources()
+    assert r5["kernel"].endswith("sbufs=3,cta_pair>") and r5["grid"] == [32, 128, 1]
+    assert r5["threads_per_cta"] == 256 and r5["tmem_cols"] == 512
     # D = 256 with BLOCK_N 128: O 256 + 2 S buffers x 128 fill TMEM (two buffers)
     r4 = compile_module("attention", (4, 512, 256), {**base, "num_stages": 1}).resources()
     assert r4["kernel"].endswith("sbufs=2>") and r4["tmem_cols"] == 512

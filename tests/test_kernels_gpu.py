@@ -178,10 +178,12 @@ def test_tcgen05_attention_shapes(shape, dtype, causal):
     inputs = O.make_inputs(name, shape, dtype, 2)
     ref = O.reference(name, inputs)
     ran = 0
-    for bn, stages, warps in [(bn, st, w) for bn in (32, 64, 128) for st in (1, 2, 3)
-                              for w in (4, 8)]:
+    # BLOCK_M 256: CTA pairs on two query tiles (odd tile counts leave the
+    # last pair's second tile partly or wholly past S)
+    for bm, bn, stages, warps in [(bm, bn, st, w) for bm in (128, 256) for bn in (32, 64, 128)
+                                  for st in (1, 2, 3) for w in (4, 8)]:
         if True:
-            cfg = {"BLOCK_M": 128, "BLOCK_N": bn, "num_warps": warps, "num_stages": stages,
+            cfg = {"BLOCK_M": bm, "BLOCK_N": bn, "num_warps": warps, "num_stages": stages,
                    "dtype": dtype}
             try:
                 out, kc = run(name, shape, cfg, inputs)
@@ -191,7 +193,7 @@ def test_tcgen05_attention_shapes(shape, dtype, causal):
             assert kc.launch["kernel"].startswith("attn_tc_kernel")
             assert_close(name, dtype, out, ref, f"{shape} {cfg}")
             ran += 1
-    assert ran >= 3
+    assert ran >= 6
 
 
 def test_edge_cases():

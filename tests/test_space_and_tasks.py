@@ -50,7 +50,7 @@ def test_b200_spaces_match_workload_definition():
     sm = get_task("softmax", "b200").param_space((16384, 8192))
     assert sm["BLOCK_N"].choices == (1024, 2048, 4096, 8192, 16384)
     at = get_task("attention_causal", "b200").param_space((128, 4096, 128))
-    assert at["BLOCK_M"].choices == (64, 128) and at["BLOCK_N"].choices == (32, 64, 128)
+    assert at["BLOCK_M"].choices == (64, 128, 256) and at["BLOCK_N"].choices == (32, 64, 128)
 
 
 def test_reference_spaces_equal_reference_sizes():
