@@ -225,6 +225,17 @@ __device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map
       : "memory");
 }
 
+// Untiled bulk copy global -> this CTA's shared memory (both addresses
+// 16-byte aligned, bytes a multiple of 16), completing on `bar`.
+__device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_t bytes,
+                                          uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::
+          "r"(dst),
+      "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(bar)
+      : "memory");
+}
+
 // Order this thread's generic-proxy shared-memory writes before later
 // async-proxy (tensor core / TMA) reads.
 __device__ __forceinline__ void fence_proxy_async_smem() {

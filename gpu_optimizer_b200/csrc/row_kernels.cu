@@ -451,6 +451,142 @@ __global__ void __launch_bounds__(1024) layernorm_rows_pipe(const T* __restrict_
   }
 }
 
+// ------------------------------------------- persistent, bulk-copy ring
+// num_stages = R >= 2 with a single register tile, 16-byte aligned rows and
+// R (+ gamma, beta) rows of shared memory: thread 0 streams whole rows into
+// an R-slot shared-memory ring with cp.async.bulk (one mbarrier per slot),
+// so R rows per CTA are in flight without holding registers, and every
+// thread reads its vector slots of the row from shared memory.  The first
+// block reduction of a row also proves that every thread has read its slot,
+// so thread 0 refills the slot with row + R * gridDim.x right after it.
+// Layernorm keeps gamma and beta in shared memory for the CTA's lifetime.
+constexpr int kRowRing = 4;
+
+template <typename T, int VPT, bool LN>
+__global__ void __launch_bounds__(1024) rows_ring(const T* __restrict__ x,
+                                                  const T* __restrict__ w,
+                                                  const T* __restrict__ b, T* __restrict__ y,
+                                                  int64_t m, int64_t n, float eps, int R,
+                                                  unsigned int* err) {
+  constexpr int V = RowVec<T>::V;
+  extern __shared__ uint8_t dsm[];
+  __shared__ uint64_t full[kRowRing];
+  __shared__ float red[32];
+  __shared__ int abort_word;
+  const uint32_t rowbytes = static_cast<uint32_t>(n) * sizeof(T);
+  const uint32_t slot = (rowbytes + 127u) & ~127u;
+  const uint32_t base = (smem_u32(dsm) + 127u) & ~127u;
+  const uint8_t* basep = dsm + (base - smem_u32(dsm));
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < R; ++s) mbar_init(smem_u32(&full[s]), 1);
+    abort_word = 0;
+    fence_barrier_init();
+  }
+  if constexpr (LN) {
+    uint4* ws = reinterpret_cast<uint4*>(const_cast<uint8_t*>(basep) + R * slot);
+    uint4* bs = reinterpret_cast<uint4*>(const_cast<uint8_t*>(basep) + (R + 1) * slot);
+    for (int64_t i = threadIdx.x; i < n / V; i += blockDim.x) {
+      ws[i] = __ldg(reinterpret_cast<const uint4*>(w) + i);
+      bs[i] = __ldg(reinterpret_cast<const uint4*>(b) + i);
+    }
+  }
+  __syncthreads();
+  volatile int* abort_flag = &abort_word;
+  int64_t row = blockIdx.x;
+  int64_t issued = 0, consumed = 0;  // rows streamed / rows taken (thread 0's view)
+  if (threadIdx.x == 0) {
+    for (int k = 0; k < R; ++k) {
+      const int64_t r = row + static_cast<int64_t>(k) * gridDim.x;
+      if (r >= m) break;
+      mbar_arrive_expect_tx(smem_u32(&full[k]), rowbytes);
+      bulk_load(base + k * slot, x + r * n, rowbytes, smem_u32(&full[k]));
+      ++issued;
+    }
+  }
+  int s = 0;
+  uint32_t ph = 0;
+  for (; row < m; row += gridDim.x) {
+    const bool ok = mbar_wait(smem_u32(&full[s]), ph, abort_flag, err, kErrWaitProducer);
+    if (!__syncthreads_and(ok)) break;
+    ++consumed;
+    uint4 raw[VPT];
+    const uint8_t* src = basep + s * slot;
+#pragma unroll
+    for (int j = 0; j < VPT; ++j) {
+      const int64_t e0 = (threadIdx.x + static_cast<int64_t>(j) * blockDim.x) * V;
+      raw[j] = e0 < n ? *reinterpret_cast<const uint4*>(src + e0 * sizeof(T))
+                      : make_uint4(0, 0, 0, 0);
+    }
+    float v[VPT * V];
+    raw_unpack<T, VPT>(raw, n, LN ? 0.f : -INFINITY, v);
+    // first reduction: its barriers also order every thread's slot read
+    // before the refill below
+    float stat = LN ? block_allreduce_sum(tree_sum(v), red) : block_allreduce_max(tree_max(v), red);
+    if (threadIdx.x == 0) {
+      const int64_t r2 = row + static_cast<int64_t>(R) * gridDim.x;
+      if (r2 < m) {
+        fence_proxy_async_smem();
+        mbar_arrive_expect_tx(smem_u32(&full[s]), rowbytes);
+        bulk_load(base + s * slot, x + r2 * n, rowbytes, smem_u32(&full[s]));
+        ++issued;
+      }
+    }
+    if constexpr (LN) {
+      const float mean = stat / static_cast<float>(n);
+      float dq[VPT * V];
+#pragma unroll
+      for (int j = 0; j < VPT; ++j) {
+        const bool in = (threadIdx.x + static_cast<int64_t>(j) * blockDim.x) * V < n;
+#pragma unroll
+        for (int u = 0; u < V; ++u) {
+          const float d = in ? v[j * V + u] - mean : 0.f;
+          dq[j * V + u] = d * d;
+        }
+      }
+      const float var = block_allreduce_sum(tree_sum(dq), red) / static_cast<float>(n);
+      const float rstd = 1.0f / sqrtf(var + eps);
+      using E = Elem<T>;
+#pragma unroll
+      for (int j = 0; j < VPT; ++j) {
+        const int64_t e0 = (threadIdx.x + static_cast<int64_t>(j) * blockDim.x) * V;
+        if (e0 < n) {
+          const uint4 wr = *reinterpret_cast<const uint4*>(basep + R * slot + e0 * sizeof(T));
+          const uint4 br = *reinterpret_cast<const uint4*>(basep + (R + 1) * slot + e0 * sizeof(T));
+          const T* we = reinterpret_cast<const T*>(&wr);
+          const T* be = reinterpret_cast<const T*>(&br);
+#pragma unroll
+          for (int u = 0; u < V; ++u)
+            v[j * V + u] = (v[j * V + u] - mean) * rstd * E::to_f(we[u]) + E::to_f(be[u]);
+        }
+      }
+    } else {
+      const float nm = -stat * 1.4426950408889634f;
+#pragma unroll
+      for (int i = 0; i < VPT * V; ++i) v[i] = exp_shifted(v[i], nm);  // padding -> 0
+      const float inv = 1.0f / block_allreduce_sum(tree_sum(v), red);
+#pragma unroll
+      for (int i = 0; i < VPT * V; ++i) v[i] *= inv;
+    }
+    raw_row_store<T, VPT>(y + row * n, n, v);
+    if (++s == R) {
+      s = 0;
+      ph ^= 1u;
+    }
+  }
+  // after an abort: let every streamed row land before the CTA exits
+  if (threadIdx.x == 0) {
+    for (int64_t i = consumed; i < issued; ++i)
+      mbar_wait_drain(smem_u32(&full[i % R]), static_cast<uint32_t>(i / R) & 1u, err);
+  }
+}
+
+// Shared memory a ring of R rows (+ gamma and beta for layernorm) needs.
+static uint32_t ring_smem(int64_t n, int es, int R, bool ln) {
+  const uint64_t slot = (static_cast<uint64_t>(n) * es + 127u) & ~uint64_t{127};
+  const uint64_t total = slot * static_cast<uint64_t>(R + (ln ? 2 : 0)) + 128u;
+  return total > kMaxSmemPerCta ? 0u : static_cast<uint32_t>(total);
+}
+
 // ------------------------------------------------------------------- host
 // Plan: aux[0] = VPT (vector slots per thread, 0 = smem-staged single tile),
 // aux[1] = single-tile flag, aux[2] = dynamic smem bytes.
@@ -494,21 +630,35 @@ static gpo_status plan_rows(const gpo_key& k, Plan& p, std::string& log, const c
   p.aux[0] = vpt;
   p.aux[1] = single ? 1 : 0;
   p.aux[2] = static_cast<int>(dyn);
-  // persistent row pipeline: register tile, single tile, aligned rows
+  // persistent row pipeline: register tile, single tile, aligned rows;
+  // a shared-memory ring of num_stages rows when it fits (aux[3] = 2),
+  // else one row prefetched into registers (aux[3] = 1)
   const bool pipe = single && vpt > 0 && k.num_stages >= 2 &&
                     (n * dtype_bytes(k.dtype)) % 16 == 0;
-  p.aux[3] = pipe ? 1 : 0;
+  const int ring_r = std::min(k.num_stages, kRowRing);
+  const uint32_t ring_dyn =
+      pipe ? ring_smem(n, dtype_bytes(k.dtype), ring_r, k.task == GPO_TASK_LAYERNORM) : 0u;
+  p.aux[3] = pipe ? (ring_dyn ? 2 : 1) : 0;
+  p.aux[4] = ring_r;
+  if (ring_dyn) {
+    dyn = ring_dyn;
+    p.aux[2] = static_cast<int>(dyn);
+  }
   p.family = "row_kernels";
   p.res.threads_per_cta = static_cast<uint32_t>(threads);
   p.res.grid_x = static_cast<uint32_t>(std::max<int64_t>(1, k.shape[0]));
   p.res.grid_y = p.res.grid_z = 1;
   p.res.launches_per_call = 1;
   p.res.smem_bytes = dyn + 128;
-  snprintf(p.res.kernel, sizeof(p.res.kernel), "%s_%s<vpt=%d>", what,
-           pipe ? "rows_pipe"
-                : single ? (vpt ? "tile_regs" : "tile_smem")
-                         : (k.task == GPO_TASK_SOFTMAX ? "online" : "twopass"),
-           vpt);
+  if (ring_dyn)
+    snprintf(p.res.kernel, sizeof(p.res.kernel), "%s_rows_ring<vpt=%d,rows=%d>", what, vpt,
+             ring_r);
+  else
+    snprintf(p.res.kernel, sizeof(p.res.kernel), "%s_%s<vpt=%d>", what,
+             pipe ? "rows_pipe"
+                  : single ? (vpt ? "tile_regs" : "tile_smem")
+                           : (k.task == GPO_TASK_SOFTMAX ? "online" : "twopass"),
+             vpt);
   if (pipe) p.res.persistent = 1;
   return GPO_OK;
 }
@@ -527,7 +677,16 @@ static gpo_status softmax_vpt(const gpo_key& k, const Plan& p, const gpo_args& a
   const int threads = k.num_warps * 32;
   const T* x = static_cast<const T*>(a.in[0]);
   T* y = static_cast<T*>(a.out);
-  if (p.aux[3] && vec) {
+  if (p.aux[3] == 2 && vec) {
+    auto kern = rows_ring<T, VPT, false>;
+    const uint32_t dyn = static_cast<uint32_t>(p.aux[2]);
+    gpo_status s = ensure_smem_attr(reinterpret_cast<const void*>(kern), dyn);
+    if (s != GPO_OK) return s;
+    const unsigned pg = persistent_grid(reinterpret_cast<const void*>(kern), threads, dyn,
+                                        c.sm_count, k.shape[0]);
+    kern<<<pg, threads, dyn, c.stream>>>(x, nullptr, nullptr, y, k.shape[0], k.shape[1], 0.f,
+                                         p.aux[4], c.err);
+  } else if (p.aux[3] && vec) {
     auto kern = softmax_rows_pipe<T, VPT>;
     const unsigned pg = persistent_grid(reinterpret_cast<const void*>(kern), threads, 0,
                                         c.sm_count, k.shape[0]);
@@ -584,7 +743,16 @@ static gpo_status layernorm_vpt(const gpo_key& k, const Plan& p, const gpo_args&
   const T* w = static_cast<const T*>(a.in[1]);
   const T* b = static_cast<const T*>(a.in[2]);
   T* y = static_cast<T*>(a.out);
-  if (p.aux[3] && vec) {
+  if (p.aux[3] == 2 && vec) {
+    auto kern = rows_ring<T, VPT, true>;
+    const uint32_t dyn = static_cast<uint32_t>(p.aux[2]);
+    gpo_status s = ensure_smem_attr(reinterpret_cast<const void*>(kern), dyn);
+    if (s != GPO_OK) return s;
+    const unsigned pg = persistent_grid(reinterpret_cast<const void*>(kern), threads, dyn,
+                                        c.sm_count, k.shape[0]);
+    kern<<<pg, threads, dyn, c.stream>>>(x, w, b, y, k.shape[0], k.shape[1], eps, p.aux[4],
+                                         c.err);
+  } else if (p.aux[3] && vec) {
     auto kern = layernorm_rows_pipe<T, VPT>;
     const unsigned pg = persistent_grid(reinterpret_cast<const void*>(kern), threads, 0,
                                         c.sm_count, k.shape[0]);

@@ -79,8 +79,12 @@ def task_configs(name, dtype):
                 for s in ("loop", "atomic", "two_pass") for b, w in ((256, 1), (8192, 16),
                                                                     (1024, 4))]
     if name in ("softmax", "layernorm"):
-        return [{"BLOCK_N": b, "num_warps": w, "num_stages": 2, "dtype": dtype}
-                for b, w in ((128, 4), (512, 1), (1024, 4), (4096, 16), (16384, 1), (256, 16))]
+        # num_stages >= 2 on single tiles: persistent row ring (shared-memory
+        # ring of num_stages rows) or, when the ring does not fit, the
+        # register prefetch pipeline
+        return [{"BLOCK_N": b, "num_warps": w, "num_stages": s, "dtype": dtype}
+                for b, w, s in ((128, 4, 2), (512, 1, 2), (1024, 4, 3), (4096, 16, 4),
+                                (16384, 1, 2), (256, 16, 2), (1024, 8, 1), (4096, 8, 4))]
     if name in ("fused_elementwise", "fused_gelu"):
         return [{"BLOCK_SIZE": b, "num_warps": w, "strategy": s, "dtype": dtype}
                 for s in ("fused", "unfused") for b, w in ((128, 1), (1024, 4), (4096, 8))]
