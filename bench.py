@@ -321,6 +321,54 @@ def cpu_baseline():
                       f"{el:.1f} s, torch CPU with {os.cpu_count()} threads"}
 
 
+# Per-task CPU samples: the reference's CPU path (the oracle's restatement of
+# each task.reference) on a bounded slice of the benchmark workload, scaled
+# to the unit of the task's roofline work.  (task, full shape, sample shape,
+# work of the sample in the task's unit numerator)
+def _cpu_samples():
+    def attn_flops(bh, s, d, causal):
+        return 4.0 * bh * d * (s * (s + 1) / 2 if causal else s * s)
+    return [
+        ("vecadd", (1 << 24,), (1 << 24,), lambda sh: 3 * sh[0] * 4),
+        ("softmax", (16384, 8192), (512, 8192), lambda sh: 2 * sh[0] * sh[1] * 2),
+        ("layernorm", (16384, 8192), (512, 8192),
+         lambda sh: 2 * sh[0] * sh[1] * 2 + 2 * sh[1] * 2),
+        ("reduction", (1 << 28,), (1 << 26,), lambda sh: 4 * sh[0]),
+        ("fused_gelu", (1 << 26,), (1 << 24,), lambda sh: 3 * sh[0] * 2),
+        ("attention_causal", (128, 4096, 128), (1, 4096, 128),
+         lambda sh: attn_flops(sh[0], sh[1], sh[2], True)),
+        ("attention", (128, 4096, 128), (1, 4096, 128),
+         lambda sh: attn_flops(sh[0], sh[1], sh[2], False)),
+        ("matmul", (8192, 8192, 8192), (128, 8192, 8192),
+         lambda sh: 2.0 * sh[0] * sh[1] * sh[2]),
+    ]
+
+
+def cpu_task_baselines():
+    """Reference CPU path per task (bounded samples, all host threads)."""
+    from oracle import reference as O
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    out = {}
+    for name, full, sample, work in _cpu_samples():
+        dtype = "float32" if name in ("vecadd", "reduction") else "bfloat16"
+        ins = O.make_inputs(name, sample, dtype, 0, profile="b200")
+        O.reference(name, ins)  # warm-up
+        times = []
+        for _ in range(3):
+            t0 = time.perf_counter()
+            O.reference(name, ins)
+            times.append(time.perf_counter() - t0)
+        t = sorted(times)[1]
+        tensor = name.startswith("attention") or name == "matmul"
+        v = work(sample) / t / (1e12 if tensor else 1e9)
+        out[f"{name}{list(full)}"] = {
+            "value": round(v, 4), "unit": "TFLOP/s" if tensor else "GB/s",
+            "cores": os.cpu_count(), "kind": "port",
+            "sample": f"{list(sample)} {dtype}, median of 3, {t * 1e3:.1f} ms"}
+    return out
+
+
 def run_reference(args, rank, world):
     if rank != 0:
         return None
@@ -444,6 +492,13 @@ def main():
             line["tasks"] = run_extras(world)
     if rank == 0 and world == 1 and not args.no_extras:
         line["cpu_baseline"] = cpu_baseline()
+        try:
+            cpu = cpu_task_baselines()
+            for k, v in cpu.items():
+                if k in line.get("tasks", {}):
+                    line["tasks"][k]["cpu_baseline"] = v
+        except Exception as e:  # keep the headline line alive
+            line["cpu_task_baselines_error"] = str(e)[:200]
     if rank == 0:
         print(json.dumps(line), flush=True)
     if world > 1:

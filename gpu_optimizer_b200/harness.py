@@ -112,6 +112,9 @@ class BenchmarkSettings:
     seed: int = 0
     flush_l2: bool = False
     cache_inputs: int = 2  # input sets kept resident per engine
+    # time replays of a CUDA graph holding one call instead of the calls
+    # themselves: removes host launch overhead from small kernels' numbers
+    cuda_graph: bool = False
 
 
 class L2Flusher:
@@ -186,11 +189,25 @@ class CudaBenchmarkEngine:
         return inputs, ref
 
     # ------------------------------------------------------------- timing
-    def _time_callable(self, fn) -> LatencyStats:
+    def _time_callable(self, fn, graph_ok: bool = True) -> LatencyStats:
         s = self.settings
         for _ in range(s.warmup):
             fn()
         torch.cuda.synchronize(self.device)
+        if s.cuda_graph and graph_ok:
+            # capture one call (every lazy setup already ran in the warm-up)
+            # on a side stream, then time graph replays on the current one
+            g = torch.cuda.CUDAGraph()
+            side = torch.cuda.Stream(self.device)
+            side.wait_stream(torch.cuda.current_stream(self.device))
+            with torch.cuda.stream(side):
+                with torch.cuda.graph(g, stream=side):
+                    fn()
+            torch.cuda.current_stream(self.device).wait_stream(side)
+            torch.cuda.synchronize(self.device)
+            fn = g.replay
+            fn()
+            torch.cuda.synchronize(self.device)
         if s.flush_l2 and self._flusher is None:
             self._flusher = L2Flusher(self.device)
         starts = [torch.cuda.Event(enable_timing=True) for _ in range(s.iterations)]
@@ -267,7 +284,7 @@ class CudaBenchmarkEngine:
                            dtype: str = "float32") -> BenchmarkResult:
         shape = tuple(int(x) for x in shape)
         inputs, _ = self.inputs_and_reference(task, shape, dtype)
-        stats = self._time_callable(lambda: task.baseline(*inputs))
+        stats = self._time_callable(lambda: task.baseline(*inputs), graph_ok=False)
         gflops = task.flops(shape) / (stats.median_ms * 1e-3) / 1e9
         ach, unit, frac = self._roofline(task, shape, dtype, stats.median_ms)
         return BenchmarkResult(

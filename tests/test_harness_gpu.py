@@ -78,3 +78,56 @@ def test_baseline_and_roofline_fields(engine):
     res = engine.benchmark_candidate(task, task.make_candidate(
         shape, {"BLOCK_SIZE": 4096, "num_warps": 8, "dtype": "float32"}))
     assert res.ok and 0 < res.roofline_fraction < 1.5
+
+
+# one config per family, including launches that zero an output (atomic
+# reduction) and multi-launch strategies (unfused elementwise, two_pass)
+GRAPH_CFGS = {
+    "matmul": {"BLOCK_M": 128, "BLOCK_N": 128, "BLOCK_K": 64, "GROUP_M": 8, "num_warps": 4,
+               "num_stages": 3, "dtype": "bfloat16"},
+    "vecadd": {"BLOCK_SIZE": 1024, "num_warps": 4, "dtype": "float32"},
+    "reduction": {"BLOCK_SIZE": 1024, "num_warps": 4, "strategy": "atomic", "dtype": "float32"},
+    "softmax": {"BLOCK_N": 1024, "num_warps": 4, "num_stages": 2, "dtype": "bfloat16"},
+    "layernorm": {"BLOCK_N": 1024, "num_warps": 4, "num_stages": 2, "dtype": "bfloat16"},
+    "fused_elementwise": {"BLOCK_SIZE": 1024, "num_warps": 4, "strategy": "unfused",
+                          "dtype": "bfloat16"},
+    "attention_causal": {"BLOCK_M": 128, "BLOCK_N": 64, "num_warps": 4, "num_stages": 2,
+                         "dtype": "bfloat16"},
+}
+
+
+@pytest.mark.parametrize("name", sorted(GRAPH_CFGS))
+def test_launches_replay_from_cuda_graph(name):
+    """Every family's launch sequence is capturable: a replayed graph gives
+    the reference's answer, and the harness times it with cuda_graph=True."""
+    import torch
+
+    from gpu_optimizer_b200.correctness import check_correctness
+    from gpu_optimizer_b200.runner import build_callable, check_device_status
+
+    task = get_task(name, "b200")
+    shape = GPU_SHAPES[name] if name != "matmul" else (512, 512, 256)
+    cfg = GRAPH_CFGS[name]
+    inputs = task.make_inputs(shape, cfg["dtype"], "cuda", 0)
+    ref = task.reference(*inputs)
+    kc = build_callable(name, shape, cfg, inputs)
+    kc.fn()
+    torch.cuda.synchronize()
+    out = kc.fn()
+    out.zero_()
+    g = torch.cuda.CUDAGraph()
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        with torch.cuda.graph(g, stream=side):
+            kc.fn()
+    torch.cuda.current_stream().wait_stream(side)
+    g.replay()
+    torch.cuda.synchronize()
+    check_device_status()
+    rtol, atol = task.tolerance(cfg["dtype"])
+    assert check_correctness(out, ref, rtol, atol).passed
+    eng = CudaBenchmarkEngine(settings=BenchmarkSettings(warmup=3, iterations=10,
+                                                         cuda_graph=True))
+    res = eng.benchmark_candidate(task, task.make_candidate(shape, cfg))
+    assert res.ok and res.latency.median_ms > 0, res.error
