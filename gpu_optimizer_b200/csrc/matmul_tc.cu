@@ -7,10 +7,13 @@
 // (runner.py:101), fp32 accumulation in TMEM.
 //
 // Config mapping (one instantiation per (dtype, BLOCK_M, BLOCK_N, warps)):
-//   BLOCK_M    : 128 -> one M=128 MMA per K step.  256 with 4 warps -> a CTA
-//                pair (cluster of 2, cta_group::2 M=256 MMAs, each CTA
-//                staging half of B; matmul_tc2_kernel).  256 with 8 warps ->
-//                two M=128 MMAs per CTA into two TMEM accumulators sharing B.
+//   BLOCK_M    : 128 -> one M=128 MMA per K step (matmul_tc_kernel).
+//                256 -> a CTA pair (cluster of 2, cta_group::2 M=256 MMAs,
+//                each CTA staging 128 rows of A and half of B;
+//                matmul_tc2_kernel), persistent with 8 warps.  tf32 with
+//                BLOCK_N 32 (a 16-column B half cannot take the 32-bit
+//                MN-major swizzle) keeps one CTA with two M=128 MMAs into two
+//                TMEM accumulators sharing B.
 //   BLOCK_N    : MMA N and TMEM columns per accumulator.
 //   BLOCK_K    : K extent of one TMA stage (runtime); the MMA issuer walks it
 //                in 32-byte K steps (16 bf16/fp16 or 8 tf32 elements).
