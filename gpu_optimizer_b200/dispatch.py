@@ -48,9 +48,15 @@ def _error_result(cand: Candidate, msg: str, worker_id: int, device: int) -> Ben
 
 
 def _worker_main(worker_id: int, device: int, pin_device: bool, factory: EngineFactory,
-                 settings: BenchmarkSettings, profile: str, conn) -> None:
+                 settings: BenchmarkSettings, profile: str, conn, host_threads: int = 0) -> None:
     if pin_device:
         os.environ["CUDA_VISIBLE_DEVICES"] = str(device)
+    if host_threads > 0:
+        # the host cores are shared by all workers: input generation and
+        # CPU-side reference work must not oversubscribe them
+        import torch
+
+        torch.set_num_threads(host_threads)
     from .tasks import get_task
 
     engine, init_err = None, ""
@@ -118,9 +124,10 @@ class MultiDeviceEvaluator:
 
     def _spawn(self, wid: int, device: int) -> _Worker:
         parent, child = self._ctx.Pipe(duplex=True)
+        threads = max(1, (os.cpu_count() or 1) // len(self.devices))
         p = self._ctx.Process(target=_worker_main, daemon=True,
                               args=(wid, device, self.pin_devices, self.factory, self.settings,
-                                    self.profile, child))
+                                    self.profile, child, threads))
         p.start()
         child.close()
         return _Worker(wid, device, p, parent)

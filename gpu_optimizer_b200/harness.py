@@ -111,7 +111,9 @@ class BenchmarkSettings:
     iterations: int = 100
     seed: int = 0
     flush_l2: bool = False
-    cache_inputs: int = 2  # input sets kept resident per engine
+    # input sets (with their reference outputs) kept resident per engine: a
+    # search draws every dtype of a task, so keep all of them
+    cache_inputs: int = 8
     # time replays of a CUDA graph holding one call instead of the calls
     # themselves: removes host launch overhead from small kernels' numbers
     cuda_graph: bool = False
