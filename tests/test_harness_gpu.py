@@ -131,3 +131,27 @@ def test_launches_replay_from_cuda_graph(name):
                                                          cuda_graph=True))
     res = eng.benchmark_candidate(task, task.make_candidate(shape, cfg))
     assert res.ok and res.latency.median_ms > 0, res.error
+
+
+def test_multi_device_evaluator_on_gpu():
+    """One spawned worker per visible GPU evaluates a small random batch and
+    returns the results in proposal order."""
+    import torch
+
+    from gpu_optimizer_b200.dispatch import MultiDeviceEvaluator
+
+    task = get_task("matmul", "b200")
+    shape = (512, 512, 512)
+    space = task.param_space(shape)
+    rng = random.Random(3)
+    cands = [task.make_candidate(shape, space.sample(rng), "random") for _ in range(6)]
+    ev = MultiDeviceEvaluator(devices=list(range(torch.cuda.device_count())), profile="b200",
+                              settings=BenchmarkSettings(warmup=2, iterations=5))
+    try:
+        assert ev.wait_ready(timeout_s=300)
+        res = ev.evaluate(cands)
+    finally:
+        ev.close()
+    assert [r.candidate_id for r in res] == [c.candidate_id for c in cands]
+    assert all(r.status in ("ok", "compile_error") for r in res), [r.error for r in res]
+    assert any(r.status == "ok" for r in res)
