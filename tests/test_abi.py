@@ -153,6 +153,30 @@ def test_row_kernel_plans():
     assert r["kernel"] == "layernorm_twopass<vpt=1>"
 
 
+def test_row_ring_plans():
+    # num_stages rows of shared memory (+ gamma, beta for layernorm)
+    r = compile_module("softmax", (16384, 8192), {"BLOCK_N": 8192, "num_warps": 8,
+                                                  "num_stages": 3,
+                                                  "dtype": "bfloat16"}).resources()
+    assert r["kernel"] == "softmax_rows_ring<vpt=4,rows=3>" and r["persistent"]
+    assert r["smem_bytes"] >= 3 * 8192 * 2
+    r = compile_module("layernorm", (16384, 8192), {"BLOCK_N": 8192, "num_warps": 16,
+                                                    "num_stages": 2,
+                                                    "dtype": "bfloat16"}).resources()
+    assert r["kernel"] == "layernorm_rows_ring<vpt=2,rows=2>"
+    assert r["smem_bytes"] >= 4 * 8192 * 2
+    # rows whose bytes are not a multiple of 16 cannot be bulk-copied: tile kernel
+    r = compile_module("softmax", (64, 1001), {"BLOCK_N": 1024, "num_warps": 4,
+                                               "num_stages": 2,
+                                               "dtype": "bfloat16"}).resources()
+    assert r["kernel"].startswith("softmax_tile_regs")
+    # a ring that does not fit shared memory falls back to the register prefetch
+    r = compile_module("layernorm", (64, 16384), {"BLOCK_N": 16384, "num_warps": 16,
+                                                  "num_stages": 4,
+                                                  "dtype": "float32"}).resources()
+    assert r["kernel"] == "layernorm_rows_pipe<vpt=8>"
+
+
 def test_cta_pair_plan():
     r = mm({"BLOCK_M": 256, "num_warps": 4, "num_stages": 3}).resources()
     assert r["kernel"] == "matmul_tc2_kernel<bf16,256,256,cta_pair>"
