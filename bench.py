@@ -42,8 +42,11 @@ FLOPS = 2.0 * SHAPE[0] * SHAPE[1] * SHAPE[2]
 N_SETS = 4
 METRIC = "matmul_bf16_4096_tflops"
 # DRAM bytes (read + write) per launch of the headline kernel from one ncu
-# capture (profiles/matmul_tc_bf16_4096.md); None until captured.
-TRAFFIC_BYTES_PER_LAUNCH = None
+# capture of this exact kernel and configuration
+# (profiles/matmul_tc2_cta_pair_bf16_4096.md: 75.19 MB read + 11.55 MB
+# written); reported only while the headline runs that kernel.
+TRAFFIC_KERNEL = "matmul_tc2_kernel<bf16,256,256,cta_pair>"
+TRAFFIC_BYTES_PER_LAUNCH = 86_740_000
 
 
 def parse_args():
@@ -219,7 +222,8 @@ def run_ours(args, rank, world, local):
                      "peak_source": "measured sustained cuBLAS bf16 (MEASURED_PEAKS.json "
                      "bf16_tflops_sustained)" if peaks["source"] == "measured"
                      else "fallback 1590 TFLOP/s (burst)",
-                     "traffic": TRAFFIC_BYTES_PER_LAUNCH,
+                     "traffic": (TRAFFIC_BYTES_PER_LAUNCH
+                                 if kcs[0].launch["kernel"] == TRAFFIC_KERNEL else None),
                      "algorithmic_flops_per_launch": FLOPS},
         "e2e": e2e,
         "gpu_launches": args.steps,
