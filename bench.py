@@ -414,7 +414,7 @@ EXTRA_TASKS = [
     ("vecadd", (1 << 24,), {"BLOCK_SIZE": 2048, "num_warps": 4, "dtype": "float32"}),
     ("softmax", (16384, 8192), {"BLOCK_N": 8192, "num_warps": 8, "num_stages": 2,
                                 "dtype": "bfloat16"}),
-    ("layernorm", (16384, 8192), {"BLOCK_N": 8192, "num_warps": 16, "num_stages": 2,
+    ("layernorm", (16384, 8192), {"BLOCK_N": 8192, "num_warps": 4, "num_stages": 2,
                                   "dtype": "bfloat16"}),
     ("reduction", (1 << 28,), {"BLOCK_SIZE": 8192, "num_warps": 16, "strategy": "atomic",
                                "dtype": "float32"}),

@@ -341,6 +341,13 @@ __global__ void __launch_bounds__(1024) layernorm_twopass(const T* __restrict__ 
 // row r it already has the raw 16-byte vectors of its next row in flight,
 // so HBM reads never wait on the block reductions.
 
+// Largest CTA of the persistent row kernels for VPT vector slots per thread:
+// four or more slots (32+ values in registers, plus the next row's vectors)
+// need more than the 64 registers a 1024-thread bound leaves, so those
+// instantiations are bounded to 256 threads and plan_rows sends wider CTAs
+// to the per-row kernels.
+__host__ __device__ constexpr int row_pipe_max_threads(int vpt) { return vpt >= 4 ? 256 : 1024; }
+
 // Raw vector slots of one row (vec path: n*sizeof(T) % 16 == 0, so a slot
 // is either fully inside the row or fully outside; outside slots read 0).
 template <typename T, int VPT>
@@ -387,7 +394,7 @@ __device__ __forceinline__ void raw_row_store(T* __restrict__ row, int64_t n,
 }
 
 template <typename T, int VPT>
-__global__ void __launch_bounds__(1024) softmax_rows_pipe(const T* __restrict__ x,
+__global__ void __launch_bounds__(row_pipe_max_threads(VPT)) softmax_rows_pipe(const T* __restrict__ x,
                                                           T* __restrict__ y, int64_t m,
                                                           int64_t n) {
   constexpr int V = RowVec<T>::V;
@@ -415,7 +422,7 @@ __global__ void __launch_bounds__(1024) softmax_rows_pipe(const T* __restrict__ 
 }
 
 template <typename T, int VPT>
-__global__ void __launch_bounds__(1024) layernorm_rows_pipe(const T* __restrict__ x,
+__global__ void __launch_bounds__(row_pipe_max_threads(VPT)) layernorm_rows_pipe(const T* __restrict__ x,
                                                             const T* __restrict__ w,
                                                             const T* __restrict__ b,
                                                             T* __restrict__ y, int64_t m,
@@ -463,7 +470,7 @@ __global__ void __launch_bounds__(1024) layernorm_rows_pipe(const T* __restrict_
 constexpr int kRowRing = 4;
 
 template <typename T, int VPT, bool LN>
-__global__ void __launch_bounds__(1024) rows_ring(const T* __restrict__ x,
+__global__ void __launch_bounds__(row_pipe_max_threads(VPT)) rows_ring(const T* __restrict__ x,
                                                   const T* __restrict__ w,
                                                   const T* __restrict__ b, T* __restrict__ y,
                                                   int64_t m, int64_t n, float eps, int R,
@@ -634,7 +641,7 @@ static gpo_status plan_rows(const gpo_key& k, Plan& p, std::string& log, const c
   // a shared-memory ring of num_stages rows when it fits (aux[3] = 2),
   // else one row prefetched into registers (aux[3] = 1)
   const bool pipe = single && vpt > 0 && k.num_stages >= 2 &&
-                    (n * dtype_bytes(k.dtype)) % 16 == 0;
+                    (n * dtype_bytes(k.dtype)) % 16 == 0 && threads <= row_pipe_max_threads(vpt);
   const int ring_r = std::min(k.num_stages, kRowRing);
   const uint32_t ring_dyn =
       pipe ? ring_smem(n, dtype_bytes(k.dtype), ring_r, k.task == GPO_TASK_LAYERNORM) : 0u;

@@ -171,10 +171,16 @@ def test_row_ring_plans():
                                                "dtype": "bfloat16"}).resources()
     assert r["kernel"].startswith("softmax_tile_regs")
     # a ring that does not fit shared memory falls back to the register prefetch
+    r = compile_module("layernorm", (64, 16384), {"BLOCK_N": 16384, "num_warps": 8,
+                                                  "num_stages": 4,
+                                                  "dtype": "float32"}).resources()
+    assert r["kernel"] == "layernorm_rows_pipe<vpt=16>"
+    # 4+ slots per thread need more than 64 registers: CTAs wider than 256
+    # threads take the per-row kernel
     r = compile_module("layernorm", (64, 16384), {"BLOCK_N": 16384, "num_warps": 16,
                                                   "num_stages": 4,
                                                   "dtype": "float32"}).resources()
-    assert r["kernel"] == "layernorm_rows_pipe<vpt=8>"
+    assert r["kernel"] == "layernorm_tile_regs<vpt=8>"
 
 
 def test_cta_pair_plan():
