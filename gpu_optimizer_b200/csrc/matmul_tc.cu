@@ -1,13 +1,17 @@
 // C = A @ B on the 5th-generation tensor cores (tcgen05) for sm_100a.
 //
 // Replaces matmul_kernel (compiler/triton/kernels.py:26-65) for 16-bit and
-// tf32 candidates whose BLOCK_M is 128 or 256.  A is M x K row-major
+// tf32 candidates whose BLOCK_M is 128 or 256 (and 16-bit ones with
+// BLOCK_M 64).  A is M x K row-major
 // (K-major operand), B is K x N row-major (MN-major operand, the layout the
 // reference passes: runner.py:107 stride_bk = N), C is M x N in A's dtype
 // (runner.py:101), fp32 accumulation in TMEM.
 //
 // Config mapping (one instantiation per (dtype, BLOCK_M, BLOCK_N, warps)):
-//   BLOCK_M    : 128 -> one M=128 MMA per K step (matmul_tc_kernel).
+//   BLOCK_M    : 64  -> one M=64 MMA per K step (16-bit only); D row
+//                16g + r sits in TMEM lane 32g + r (g < 4, r < 16), so each
+//                epilogue warp stores 16 rows.
+//                128 -> one M=128 MMA per K step (matmul_tc_kernel).
 //                256 -> a CTA pair (cluster of 2, cta_group::2 M=256 MMAs,
 //                each CTA staging 128 rows of A and half of B;
 //                matmul_tc2_kernel), persistent with 8 warps.  tf32 with
@@ -124,7 +128,10 @@ __global__ void __launch_bounds__(PERSISTENT ? 256 : 128, 1)
                      int K, int BK, int stages, int group_m, int swa, unsigned int* err) {
   constexpr int ES = sizeof(T);
   constexpr int SWB = (BN * ES) < 128 ? (BN * ES) : 128;
-  constexpr int HALVES = BM / 128;
+  // BLOCK_M 64: one M=64 MMA per K step; its D rows 16g..16g+15 land in
+  // TMEM lanes 32g..32g+15 (g = 0..3), columns as N (measured layout)
+  constexpr int MMA_M = BM < 128 ? BM : 128;
+  constexpr int HALVES = BM < 128 ? 1 : BM / 128;
   constexpr int COLS = HALVES * BN;  // TMEM columns per accumulator buffer
   constexpr int ACC_STAGES = (PERSISTENT && 2 * COLS <= 512) ? 2 : 1;
   constexpr int ALLOC = (ACC_STAGES * COLS) <= 32    ? 32
@@ -133,7 +140,7 @@ __global__ void __launch_bounds__(PERSISTENT ? 256 : 128, 1)
                         : (ACC_STAGES * COLS) <= 256 ? 256
                                                      : 512;
   constexpr int KSTEP = 32 / ES;  // K elements per MMA instruction
-  constexpr uint32_t IDESC = make_idesc(FMT, 128, BN, false, true);
+  constexpr uint32_t IDESC = make_idesc(FMT, MMA_M, BN, false, true);
 
   __shared__ TcShared sh;
   extern __shared__ uint8_t dyn_smem[];
@@ -282,7 +289,9 @@ __global__ void __launch_bounds__(PERSISTENT ? 256 : 128, 1)
       tile_coords(tile, num_pid_m, num_pid_n, group_m, pm, pn);
 #pragma unroll
       for (int h = 0; h < HALVES; ++h) {
-        const int row = pm * BM + h * 128 + q * 32 + lane;
+        // BLOCK_M 64: lanes 16..31 of each quarter hold no row
+        const int row = BM < 128 ? (lane < 16 ? pm * BM + q * 16 + lane : M)
+                                 : pm * BM + h * 128 + q * 32 + lane;
 #pragma unroll 1
         for (int c = 0; c < BN / 32; ++c) {
           uint32_t r[32];
@@ -610,8 +619,8 @@ gpo_status plan_matmul_tc(const gpo_key& k, Plan& p, std::string& log) {
   const int es = dtype_bytes(k.dtype);
   const int BM = k.block_m, BN = k.block_n, BK = k.block_k;
   const int64_t M = k.shape[0], N = k.shape[1], K = k.shape[2];
-  if (BM != 128 && BM != 256) {
-    log = "tcgen05 family needs BLOCK_M 128 or 256";
+  if ((BM != 64 || k.dtype == GPO_TF32) && BM != 128 && BM != 256) {
+    log = "tcgen05 family needs BLOCK_M 128 or 256 (or 64 for 16-bit inputs)";
     return GPO_BAD_CONFIG;
   }
   if (BN != 32 && BN != 64 && BN != 128 && BN != 256) {
@@ -687,7 +696,7 @@ gpo_status plan_matmul_tc(const gpo_key& k, Plan& p, std::string& log) {
   const uint32_t stage = (a_bytes + b_bytes + 1023u) & ~1023u;
   const uint32_t dyn = stage * static_cast<uint32_t>(k.num_stages) + 1024u;
   const uint32_t smem = dyn + static_cast<uint32_t>(sizeof(TcShared));
-  const int cols = (BM / 128) * BN;
+  const int cols = std::max(1, BM / 128) * BN;
   const int acc_stages = (persistent && 2 * cols <= 512) ? 2 : 1;
   int alloc = 32;
   while (alloc < acc_stages * cols) alloc *= 2;
@@ -804,6 +813,11 @@ static gpo_status run_tc_dt(const gpo_key& k, const Plan& p, const gpo_args& a,
                             const LaunchCtx& c, CUtensorMapDataType dt) {
   if (p.aux[3]) return run_tc2_bn<T, FMT>(k, p, a, c, dt);
   const bool P = p.aux[2] != 0;
+  if constexpr (FMT != 2) {
+    if (k.block_m == 64)
+      return P ? run_tc_bn<T, FMT, 64, true>(k, p, a, c, dt)
+               : run_tc_bn<T, FMT, 64, false>(k, p, a, c, dt);
+  }
   if (k.block_m == 128)
     return P ? run_tc_bn<T, FMT, 128, true>(k, p, a, c, dt)
              : run_tc_bn<T, FMT, 128, false>(k, p, a, c, dt);

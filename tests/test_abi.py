@@ -53,6 +53,18 @@ def test_tcgen05_matmul_plan():
     assert res4["grid"][0] == 32 * 16
 
 
+def test_block_m_64_uses_m64_tensor_core_mmas_for_16_bit_inputs():
+    res = mm({"BLOCK_M": 64, "BLOCK_N": 128, "num_warps": 4}).resources()
+    assert res["kernel"] == "matmul_tc_kernel<bf16,64,128,tile>"
+    assert res["tmem_cols"] == 128 and res["grid"][0] == 64 * 32
+    resp = mm({"BLOCK_M": 64, "BLOCK_N": 256}).resources()
+    assert resp["kernel"] == "matmul_tc_kernel<bf16,64,256,persistent>"
+    assert resp["tmem_cols"] == 512
+    # tf32 keeps M >= 128 MMAs: BLOCK_M 64 runs on the CUDA cores
+    rt = mm({"BLOCK_M": 64, "BLOCK_N": 64, "num_warps": 4, "dtype": "tf32"}).resources()
+    assert rt["kernel"].startswith("matmul_simt")
+
+
 def test_shared_memory_overflow_is_a_compile_error():
     with pytest.raises(KernelBuildError) as ei:
         mm({"BLOCK_M": 256, "BLOCK_N": 256, "BLOCK_K": 128, "num_stages": 6})
