@@ -412,7 +412,7 @@ def run_reference(args, rank, world):
 # ------------------------------------------------------------ extras
 EXTRA_TASKS = [
     ("vecadd", (1 << 24,), {"BLOCK_SIZE": 2048, "num_warps": 4, "dtype": "float32"}),
-    ("softmax", (16384, 8192), {"BLOCK_N": 8192, "num_warps": 8, "num_stages": 2,
+    ("softmax", (16384, 8192), {"BLOCK_N": 8192, "num_warps": 4, "num_stages": 2,
                                 "dtype": "bfloat16"}),
     ("layernorm", (16384, 8192), {"BLOCK_N": 8192, "num_warps": 4, "num_stages": 2,
                                   "dtype": "bfloat16"}),

@@ -458,6 +458,66 @@ __global__ void __launch_bounds__(row_pipe_max_threads(VPT)) layernorm_rows_pipe
   }
 }
 
+// Element pair p (elements 2p and 2p+1) of a 16-byte vector, as fp32.  A
+// bf16 value is the upper half of the fp32 with the same bits, so each
+// unpacks with one shift or mask.
+template <typename T>
+__device__ __forceinline__ float2 unpack2(const uint4& r, int p);
+template <>
+__device__ __forceinline__ float2 unpack2<__nv_bfloat16>(const uint4& r, int p) {
+  const uint32_t w = (&r.x)[p];
+  return make_float2(__uint_as_float(w << 16), __uint_as_float(w & 0xffff0000u));
+}
+template <>
+__device__ __forceinline__ float2 unpack2<__half>(const uint4& r, int p) {
+  const uint32_t w = (&r.x)[p];
+  return __half22float2(*reinterpret_cast<const __half2*>(&w));
+}
+template <>
+__device__ __forceinline__ float2 unpack2<float>(const uint4& r, int p) {
+  return make_float2(__uint_as_float((&r.x)[2 * p]), __uint_as_float((&r.x)[2 * p + 1]));
+}
+
+// Round an fp32 pair to T and place it as elements 2p, 2p+1 of a vector.
+template <typename T>
+__device__ __forceinline__ void pack2(uint4& r, int p, float2 y);
+template <>
+__device__ __forceinline__ void pack2<__nv_bfloat16>(uint4& r, int p, float2 y) {
+  const __nv_bfloat162 h = __floats2bfloat162_rn(y.x, y.y);
+  (&r.x)[p] = *reinterpret_cast<const uint32_t*>(&h);
+}
+template <>
+__device__ __forceinline__ void pack2<__half>(uint4& r, int p, float2 y) {
+  const __half2 h = __floats2half2_rn(y.x, y.y);
+  (&r.x)[p] = *reinterpret_cast<const uint32_t*>(&h);
+}
+template <>
+__device__ __forceinline__ void pack2<float>(uint4& r, int p, float2 y) {
+  (&r.x)[2 * p] = __float_as_uint(y.x);
+  (&r.x)[2 * p + 1] = __float_as_uint(y.y);
+}
+
+// Sums of two values over the block in one exchange; every thread receives
+// both.
+__device__ __forceinline__ float2 block_allreduce_sum2(float2 v, float2* red2) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    v.x += __shfl_xor_sync(0xffffffffu, v.x, o);
+    v.y += __shfl_xor_sync(0xffffffffu, v.y, o);
+  }
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31, nw = blockDim.x >> 5;
+  __syncthreads();
+  if (l == 0) red2[w] = v;
+  __syncthreads();
+  float2 r = l < nw ? red2[l] : make_float2(0.f, 0.f);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    r.x += __shfl_xor_sync(0xffffffffu, r.x, o);
+    r.y += __shfl_xor_sync(0xffffffffu, r.y, o);
+  }
+  return r;
+}
+
 // ------------------------------------------- persistent, bulk-copy ring
 // num_stages = R >= 2 with a single register tile, 16-byte aligned rows and
 // R (+ gamma, beta) rows of shared memory: thread 0 streams whole rows into
@@ -466,7 +526,14 @@ __global__ void __launch_bounds__(row_pipe_max_threads(VPT)) layernorm_rows_pipe
 // thread reads its vector slots of the row from shared memory.  The first
 // block reduction of a row also proves that every thread has read its slot,
 // so thread 0 refills the slot with row + R * gridDim.x right after it.
-// Layernorm keeps gamma and beta in shared memory for the CTA's lifetime.
+// Layernorm keeps gamma and beta in shared memory for the CTA's lifetime
+// and takes the row statistics in one pass: sums of d = x - x0 and d^2
+// with x0 the row's first element (the shifted-data variance, exact in
+// real arithmetic and free of the E[x^2] - E[x]^2 cancellation as long as
+// x0 lies within a few standard deviations of the mean, which a sample of
+// the row does), so each row needs one block reduction of two values
+// instead of the two dependent reductions of the two-pass form; the math
+// runs on packed fp32x2 instructions.
 constexpr int kRowRing = 4;
 
 template <typename T, int VPT, bool LN>
@@ -479,6 +546,7 @@ __global__ void __launch_bounds__(row_pipe_max_threads(VPT)) rows_ring(const T* 
   extern __shared__ uint8_t dsm[];
   __shared__ uint64_t full[kRowRing];
   __shared__ float red[32];
+  __shared__ float2 red2[32];
   __shared__ int abort_word;
   const uint32_t rowbytes = static_cast<uint32_t>(n) * sizeof(T);
   const uint32_t slot = (rowbytes + 127u) & ~127u;
@@ -512,6 +580,18 @@ __global__ void __launch_bounds__(row_pipe_max_threads(VPT)) rows_ring(const T* 
   }
   int s = 0;
   uint32_t ph = 0;
+  // thread 0 streams row + R * gridDim.x into the slot just read by all
+  auto refill = [&]() {
+    if (threadIdx.x == 0) {
+      const int64_t r2 = row + static_cast<int64_t>(R) * gridDim.x;
+      if (r2 < m) {
+        fence_proxy_async_smem();
+        mbar_arrive_expect_tx(smem_u32(&full[s]), rowbytes);
+        bulk_load(base + s * slot, x + r2 * n, rowbytes, smem_u32(&full[s]));
+        ++issued;
+      }
+    }
+  };
   for (; row < m; row += gridDim.x) {
     const bool ok = mbar_wait(smem_u32(&full[s]), ph, abort_flag, err, kErrWaitProducer);
     if (!__syncthreads_and(ok)) break;
@@ -524,57 +604,103 @@ __global__ void __launch_bounds__(row_pipe_max_threads(VPT)) rows_ring(const T* 
       raw[j] = e0 < n ? *reinterpret_cast<const uint4*>(src + e0 * sizeof(T))
                       : make_uint4(0, 0, 0, 0);
     }
-    float v[VPT * V];
-    raw_unpack<T, VPT>(raw, n, LN ? 0.f : -INFINITY, v);
-    // first reduction: its barriers also order every thread's slot read
-    // before the refill below
-    float stat = LN ? block_allreduce_sum(tree_sum(v), red) : block_allreduce_max(tree_max(v), red);
-    if (threadIdx.x == 0) {
-      const int64_t r2 = row + static_cast<int64_t>(R) * gridDim.x;
-      if (r2 < m) {
-        fence_proxy_async_smem();
-        mbar_arrive_expect_tx(smem_u32(&full[s]), rowbytes);
-        bulk_load(base + s * slot, x + r2 * n, rowbytes, smem_u32(&full[s]));
-        ++issued;
-      }
-    }
     if constexpr (LN) {
-      const float mean = stat / static_cast<float>(n);
-      float dq[VPT * V];
+      constexpr int P = V / 2;  // fp32 pairs per vector slot
+      const float x0 = Elem<T>::to_f(*reinterpret_cast<const T*>(src));
+      const float2 nx0 = make_float2(-x0, -x0);
+      float2 xv[VPT * P];
+      float2 sacc[4], qacc[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) sacc[i] = qacc[i] = make_float2(0.f, 0.f);
 #pragma unroll
       for (int j = 0; j < VPT; ++j) {
         const bool in = (threadIdx.x + static_cast<int64_t>(j) * blockDim.x) * V < n;
 #pragma unroll
-        for (int u = 0; u < V; ++u) {
-          const float d = in ? v[j * V + u] - mean : 0.f;
-          dq[j * V + u] = d * d;
+        for (int u = 0; u < P; ++u) {
+          xv[j * P + u] = unpack2<T>(raw[j], u);
+          if (in) {
+            const float2 d = __fadd2_rn(xv[j * P + u], nx0);
+            sacc[(j * P + u) & 3] = __fadd2_rn(sacc[(j * P + u) & 3], d);
+            qacc[(j * P + u) & 3] = __ffma2_rn(d, d, qacc[(j * P + u) & 3]);
+          }
         }
       }
-      const float var = block_allreduce_sum(tree_sum(dq), red) / static_cast<float>(n);
+      const float2 s01 = __fadd2_rn(sacc[0], sacc[1]), s23 = __fadd2_rn(sacc[2], sacc[3]);
+      const float2 q01 = __fadd2_rn(qacc[0], qacc[1]), q23 = __fadd2_rn(qacc[2], qacc[3]);
+      const float2 ss = __fadd2_rn(s01, s23), qq = __fadd2_rn(q01, q23);
+      // the reduction's barriers order every thread's slot read before the
+      // refill below
+      const float2 sq = block_allreduce_sum2(make_float2(ss.x + ss.y, qq.x + qq.y), red2);
+      refill();
+      const float inv_n = 1.0f / static_cast<float>(n);
+      const float dm = sq.x * inv_n;  // mean of d
+      const float mean = x0 + dm;
+      const float var = fmaxf(fmaf(-dm, dm, sq.y * inv_n), 0.f);
       const float rstd = 1.0f / sqrtf(var + eps);
-      using E = Elem<T>;
+      const float2 nmean = make_float2(-mean, -mean), rstd2 = make_float2(rstd, rstd);
 #pragma unroll
       for (int j = 0; j < VPT; ++j) {
         const int64_t e0 = (threadIdx.x + static_cast<int64_t>(j) * blockDim.x) * V;
         if (e0 < n) {
           const uint4 wr = *reinterpret_cast<const uint4*>(basep + R * slot + e0 * sizeof(T));
           const uint4 br = *reinterpret_cast<const uint4*>(basep + (R + 1) * slot + e0 * sizeof(T));
-          const T* we = reinterpret_cast<const T*>(&wr);
-          const T* be = reinterpret_cast<const T*>(&br);
+          uint4 o;
 #pragma unroll
-          for (int u = 0; u < V; ++u)
-            v[j * V + u] = (v[j * V + u] - mean) * rstd * E::to_f(we[u]) + E::to_f(be[u]);
+          for (int u = 0; u < P; ++u) {
+            const float2 t = __fmul2_rn(__fadd2_rn(xv[j * P + u], nmean), rstd2);
+            pack2<T>(o, u, __ffma2_rn(t, unpack2<T>(wr, u), unpack2<T>(br, u)));
+          }
+          __stcs(reinterpret_cast<uint4*>(y + row * n + e0), o);
         }
       }
     } else {
-      const float nm = -stat * 1.4426950408889634f;
+      constexpr int P = V / 2;
+      float2 xv[VPT * P];
+      float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
-      for (int i = 0; i < VPT * V; ++i) v[i] = exp_shifted(v[i], nm);  // padding -> 0
-      const float inv = 1.0f / block_allreduce_sum(tree_sum(v), red);
+      for (int j = 0; j < VPT; ++j) {
+        const bool in = (threadIdx.x + static_cast<int64_t>(j) * blockDim.x) * V < n;
 #pragma unroll
-      for (int i = 0; i < VPT * V; ++i) v[i] *= inv;
+        for (int u = 0; u < P; ++u) {
+          xv[j * P + u] = unpack2<T>(raw[j], u);
+          if (in) mx4[(j * P + u) & 3] = fmax3(mx4[(j * P + u) & 3], xv[j * P + u].x, xv[j * P + u].y);
+        }
+      }
+      // first reduction: its barriers also order every thread's slot read
+      // before the refill below
+      const float mx = block_allreduce_max(fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3])), red);
+      refill();
+      // exp(x - mx) = 2^(x * log2 e - mx * log2 e): one packed FMA per pair
+      // and one ex2 per element
+      const float2 l2e = make_float2(1.4426950408889634f, 1.4426950408889634f);
+      const float2 nm = make_float2(-mx * 1.4426950408889634f, -mx * 1.4426950408889634f);
+      float2 sacc[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) sacc[i] = make_float2(0.f, 0.f);
+#pragma unroll
+      for (int j = 0; j < VPT; ++j) {
+        const bool in = (threadIdx.x + static_cast<int64_t>(j) * blockDim.x) * V < n;
+#pragma unroll
+        for (int u = 0; u < P; ++u) {
+          const float2 t = __ffma2_rn(xv[j * P + u], l2e, nm);
+          xv[j * P + u] = make_float2(ex2_approx(t.x), ex2_approx(t.y));
+          if (in) sacc[(j * P + u) & 3] = __fadd2_rn(sacc[(j * P + u) & 3], xv[j * P + u]);
+        }
+      }
+      const float2 s2 = __fadd2_rn(__fadd2_rn(sacc[0], sacc[1]), __fadd2_rn(sacc[2], sacc[3]));
+      const float inv = 1.0f / block_allreduce_sum(s2.x + s2.y, red);
+      const float2 inv2 = make_float2(inv, inv);
+#pragma unroll
+      for (int j = 0; j < VPT; ++j) {
+        const int64_t e0 = (threadIdx.x + static_cast<int64_t>(j) * blockDim.x) * V;
+        if (e0 < n) {
+          uint4 o;
+#pragma unroll
+          for (int u = 0; u < P; ++u) pack2<T>(o, u, __fmul2_rn(xv[j * P + u], inv2));
+          __stcs(reinterpret_cast<uint4*>(y + row * n + e0), o);
+        }
+      }
     }
-    raw_row_store<T, VPT>(y + row * n, n, v);
     if (++s == R) {
       s = 0;
       ph ^= 1u;
