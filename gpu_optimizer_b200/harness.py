@@ -203,10 +203,6 @@ class CudaBenchmarkEngine:
             side = torch.cuda.Stream(self.device)
             side.wait_stream(torch.cuda.current_stream(self.device))
             with torch.cuda.stream(side):
-                # one uncaptured call on the capture stream first: per-stream
-                # scratch (stream-K partial tiles) is allocated on first use
-                fn()
-                side.synchronize()
                 with torch.cuda.graph(g, stream=side):
                     fn()
             torch.cuda.current_stream(self.device).wait_stream(side)
