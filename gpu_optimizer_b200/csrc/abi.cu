@@ -5,7 +5,6 @@
 #include <algorithm>
 #include <cstring>
 #include <map>
-#include <tuple>
 #include <mutex>
 #include <string>
 #include <utility>
@@ -127,11 +126,11 @@ gpo_status ensure_smem_attr(const void* func, uint32_t dyn_smem) {
 unsigned persistent_grid(const void* func, int threads, size_t dyn_smem, int sm_count,
                          int64_t work_items) {
   static std::mutex mu;
-  static std::map<std::tuple<const void*, int, size_t>, int> occ;
+  static std::map<std::pair<const void*, int>, int> occ;
   int per_sm = 0;
   {
     std::lock_guard<std::mutex> lk(mu);
-    auto it = occ.find({func, threads, dyn_smem});
+    auto it = occ.find({func, threads});
     if (it != occ.end()) per_sm = it->second;
   }
   if (per_sm == 0) {
@@ -142,7 +141,7 @@ unsigned persistent_grid(const void* func, int threads, size_t dyn_smem, int sm_
       per_sm = 1;
     }
     std::lock_guard<std::mutex> lk(mu);
-    occ[{func, threads, dyn_smem}] = per_sm;
+    occ[{func, threads}] = per_sm;
   }
   const int64_t g = static_cast<int64_t>(per_sm) * (sm_count > 0 ? sm_count : 148);
   return static_cast<unsigned>(std::max<int64_t>(1, std::min<int64_t>(g, work_items)));
@@ -150,11 +149,11 @@ unsigned persistent_grid(const void* func, int threads, size_t dyn_smem, int sm_
 
 unsigned persistent_clusters(const void* func, int threads, size_t dyn_smem, int64_t work_items) {
   static std::mutex mu;
-  static std::map<std::tuple<const void*, int, size_t>, int> occ;
+  static std::map<std::pair<const void*, int>, int> occ;
   int clusters = 0;
   {
     std::lock_guard<std::mutex> lk(mu);
-    auto it = occ.find({func, threads, dyn_smem});
+    auto it = occ.find({func, threads});
     if (it != occ.end()) clusters = it->second;
   }
   if (clusters == 0) {
@@ -167,54 +166,9 @@ unsigned persistent_clusters(const void* func, int threads, size_t dyn_smem, int
       clusters = 1;
     }
     std::lock_guard<std::mutex> lk(mu);
-    occ[{func, threads, dyn_smem}] = clusters;
+    occ[{func, threads}] = clusters;
   }
   return static_cast<unsigned>(std::max<int64_t>(1, std::min<int64_t>(clusters, work_items)));
-}
-
-gpo_status sk_workspace(const LaunchCtx& c, size_t bytes, size_t nflags, float** ws,
-                        unsigned int** flags) {
-  struct Scratch {
-    void* ws = nullptr;
-    size_t bytes = 0;
-    unsigned int* flags = nullptr;
-    size_t nflags = 0;
-  };
-  static std::mutex mu;
-  static std::map<std::pair<int, cudaStream_t>, Scratch> scratch;
-  std::lock_guard<std::mutex> lk(mu);
-  Scratch& sc = scratch[{c.device, c.stream}];
-  if (sc.bytes < bytes || sc.nflags < nflags) {
-    // a launch being captured into a graph cannot allocate: the first
-    // launch on a stream must run outside a capture
-    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
-    if (cudaStreamIsCapturing(c.stream, &cs) != cudaSuccess ||
-        cs != cudaStreamCaptureStatusNone) {
-      cudaGetLastError();
-      return GPO_LAUNCH_ERROR;
-    }
-    // grown buffers are kept, not freed: graphs captured earlier may still
-    // hold the old pointers
-    const size_t nb = std::max(bytes, sc.bytes), nf = std::max(nflags, sc.nflags);
-    void* w = nullptr;
-    void* f = nullptr;
-    if (cudaMalloc(&w, nb) != cudaSuccess) {
-      cudaGetLastError();
-      return GPO_LAUNCH_ERROR;
-    }
-    if (cudaMalloc(&f, nf * sizeof(unsigned int)) != cudaSuccess ||
-        cudaMemsetAsync(f, 0, nf * sizeof(unsigned int), c.stream) != cudaSuccess) {
-      cudaGetLastError();
-      return GPO_LAUNCH_ERROR;
-    }
-    sc.ws = w;
-    sc.bytes = nb;
-    sc.flags = static_cast<unsigned int*>(f);
-    sc.nflags = nf;
-  }
-  *ws = static_cast<float*>(sc.ws);
-  *flags = sc.flags;
-  return GPO_OK;
 }
 
 void* tensor_map_encoder() {

@@ -73,6 +73,11 @@ __host__ __device__ constexpr int attn_tmem_alloc(int cols) {
   return cols <= 32 ? 32 : cols <= 64 ? 64 : cols <= 128 ? 128 : cols <= 256 ? 256 : 512;
 }
 
+// Barrier `id` (1..15) among `count` threads (whole warps).
+__device__ __forceinline__ void named_barrier(uint32_t id, uint32_t count) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+
 // TMEM load / store of C consecutive 32-bit columns (C = 16 or 32).
 template <int C>
 __device__ __forceinline__ void tmem_ld_cols(uint32_t taddr, uint32_t* r) {

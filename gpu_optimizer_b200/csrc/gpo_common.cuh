@@ -57,7 +57,6 @@ enum : uint32_t {
   kErrWaitDrain = 1u << 4,
   kErrBadLaunch = 1u << 5,
   kErrSelfTest = 1u << 6,
-  kErrWaitPartial = 1u << 7,  // a stream-K tile waited too long for a partial
 };
 
 constexpr unsigned long long kWaitLimitNs = 2000000000ull;  // 2 s per wait
@@ -184,44 +183,6 @@ __device__ __forceinline__ bool mbar_wait_for(uint32_t bar, uint32_t parity, uns
     if ((it & 255u) == 0 && globaltimer_ns() - t0 > limit_ns) {
       atomicOr(err, site);
       return false;
-    }
-  }
-}
-
-// Barrier `id` (1..15) over `count` threads (a multiple of 32).
-__device__ __forceinline__ void named_barrier(uint32_t id, uint32_t count) {
-  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
-}
-
-// Global-memory flags between CTAs of one grid (stream-K partial tiles).
-__device__ __forceinline__ unsigned int ld_acquire_gpu(const unsigned int* p) {
-  unsigned int v;
-  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
-__device__ __forceinline__ void st_release_gpu(unsigned int* p, unsigned int v) {
-  asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-
-// Bounded wait for a flag another CTA of the grid raises (release store)
-// while it runs; polls with __nanosleep back-off.  The flag's writer never
-// waits on the caller, so the wait ends once that CTA is resident.
-__device__ __forceinline__ bool flag_wait(const unsigned int* f, volatile int* abort,
-                                          unsigned int* err, uint32_t site) {
-  if (ld_acquire_gpu(f) != 0u) return true;
-  const unsigned long long t0 = globaltimer_ns();
-  unsigned ns = 64;
-  for (uint32_t it = 1;; ++it) {
-    __nanosleep(ns);
-    if (ns < 1024) ns <<= 1;
-    if (ld_acquire_gpu(f) != 0u) return true;
-    if ((it & 15u) == 0) {
-      if (*abort) return false;
-      if (globaltimer_ns() - t0 > kWaitLimitNs) {
-        atomicOr(err, site);
-        *abort = 1;
-        return false;
-      }
     }
   }
 }

@@ -90,13 +90,6 @@ unsigned persistent_grid(const void* func, int threads, size_t dyn_smem, int sm_
 // device, capped at work_items (cached per kernel).
 unsigned persistent_clusters(const void* func, int threads, size_t dyn_smem, int64_t work_items);
 
-// Stream-K scratch of the CTA-pair matmul for the launch's (device, stream):
-// at least `bytes` of fp32 partial tiles and `nflags` flags that are zero
-// between launches.  Allocated on first use (not inside a stream capture)
-// and kept for the process.
-gpo_status sk_workspace(const LaunchCtx& c, size_t bytes, size_t nflags, float** ws,
-                        unsigned int** flags);
-
 // Driver entry point for cuTensorMapEncodeTiled, resolved once.
 void* tensor_map_encoder();
 

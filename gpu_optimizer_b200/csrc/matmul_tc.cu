@@ -340,61 +340,6 @@ __global__ void __launch_bounds__(PERSISTENT ? 256 : 128, 1)
   if (warp == alloc_warp) tmem_dealloc(tmem_base, ALLOC);
 }
 
-// Work items of one cluster of the pair kernel.  Data-parallel tiles first:
-// tile = cluster + j * clusters while tile < dp_tiles, every K block.  With
-// stream-K (dp_tiles < num_tiles) the cluster then takes its contiguous
-// share [s_c, s_{c+1}) of the (num_tiles - dp_tiles) * num_kb K-block
-// iterations of the remaining tiles, s_c = iters * c / clusters, cut at tile
-// boundaries: every cluster does the same number of K blocks, so the last,
-// partly filled wave of tiles is spread over all SMs.  A share starts inside
-// at most one tile (that part goes to the tile's finisher as an fp32
-// partial) and ends in at most one tile whose K block 0 it holds (it
-// finishes that tile: waits for the later clusters' partials, adds them and
-// stores C).
-struct PairWork {
-  int tile = 0, kb0 = 0, kb1 = 0;  // current item: K blocks [kb0, kb1) of tile
-  int next_dp, dp_tiles, clusters, num_kb;
-  int64_t sk_iters, it, end;
-  __device__ PairWork(int cluster, int clusters_, int num_tiles, int dp, int kbs)
-      : next_dp(cluster), dp_tiles(dp), clusters(clusters_), num_kb(kbs) {
-    sk_iters = static_cast<int64_t>(num_tiles - dp) * kbs;
-    it = share_begin(cluster);
-    end = share_begin(cluster + 1);
-  }
-  __device__ int64_t share_begin(int c) const { return sk_iters * c / clusters; }
-  __device__ bool next() {
-    if (next_dp < dp_tiles) {
-      tile = next_dp;
-      kb0 = 0;
-      kb1 = num_kb;
-      next_dp += clusters;
-      return true;
-    }
-    if (it < end) {
-      const int64_t u = it / num_kb;
-      const int64_t stop = min(end, (u + 1) * num_kb);
-      tile = dp_tiles + static_cast<int>(u);
-      kb0 = static_cast<int>(it - u * num_kb);
-      kb1 = static_cast<int>(stop - u * num_kb);
-      it = stop;
-      return true;
-    }
-    return false;
-  }
-};
-
-// All `count` threads of barrier `id` learn whether `v` held for all of them.
-__device__ __forceinline__ bool named_barrier_and(uint32_t id, uint32_t count, bool v) {
-  uint32_t r;
-  asm volatile(
-      "{\n .reg .pred p, q;\n setp.ne.u32 p, %1, 0;\n bar.red.and.pred q, %2, %3, p;\n"
-      " selp.u32 %0, 1, 0, q;\n}"
-      : "=r"(r)
-      : "r"(static_cast<uint32_t>(v)), "r"(id), "r"(count)
-      : "memory");
-  return r != 0;
-}
-
 // --------------------------------------------------- CTA-pair (2-SM) tile
 // BLOCK_M = 256: a cluster of two CTAs computes one 256 x BLOCK_N tile with
 // M=256 tcgen05 MMAs issued by the even CTA (cta_group::2).  CTA r holds A
@@ -419,19 +364,15 @@ __device__ __forceinline__ bool named_barrier_and(uint32_t id, uint32_t count, b
 // commits to its own and (through the cluster address) to the peer's.
 // All waits are bounded; a CTA that gives up drains and still reaches the
 // final cluster barrier, so neither CTA exits while the other can signal it.
-template <typename T, int FMT, int BN, bool PERSISTENT, bool SK = false>
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PERSISTENT ? 256 : 128, SK ? 2 : 1)
+template <typename T, int FMT, int BN, bool PERSISTENT>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PERSISTENT ? 256 : 128, 1)
     matmul_tc2_kernel(const __grid_constant__ CUtensorMap tma_a,
                       const __grid_constant__ CUtensorMap tma_b, T* __restrict__ C, int M, int N,
-                      int K, int BK, int stages, int group_m, int swa, unsigned int* err,
-                      float* __restrict__ ws, unsigned int* __restrict__ flags, int dp_tiles) {
-  static_assert(!SK || PERSISTENT, "stream-K runs on the persistent pair");
+                      int K, int BK, int stages, int group_m, int swa, unsigned int* err) {
   constexpr int ES = sizeof(T);
   constexpr int BNH = BN / 2;                                 // B columns per CTA
   constexpr int SWB = (BNH * ES) < 128 ? (BNH * ES) : 128;    // B chunk width (bytes)
-  // TMEM accumulator buffers: stream-K keeps one so that two CTAs share an
-  // SM (the co-resident cluster hides each epilogue)
-  constexpr int ACC = (PERSISTENT && !SK) ? 2 : 1;
+  constexpr int ACC = PERSISTENT ? 2 : 1;                     // TMEM accumulator buffers
   constexpr int ALLOC = tc2_tmem_alloc(ACC * BN);
   constexpr int KSTEP = 32 / ES;
   constexpr uint32_t IDESC = make_idesc(FMT, 256, BN, false, true);
@@ -448,10 +389,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PERSISTENT ? 256 : 1
   const int num_pid_m = (M + 255) / 256;
   const int num_pid_n = (N + BN - 1) / BN;
   const int num_tiles = num_pid_m * num_pid_n;
-  const int cluster = static_cast<int>(blockIdx.x >> 1);
-  const int clusters = static_cast<int>(gridDim.x >> 1);
+  const int first_tile = static_cast<int>(blockIdx.x >> 1);
+  const int tile_step = PERSISTENT ? static_cast<int>(gridDim.x >> 1) : num_tiles;
   const int num_kb = (K + BK - 1) / BK;
-  if (!SK) dp_tiles = num_tiles;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < stages; ++s) {
@@ -484,11 +424,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PERSISTENT ? 256 : 1
     int it = 0, s = 0;  // K blocks issued; ring slot and phase of the next one
     uint32_t ph = 0;
     bool ok = true;
-    PairWork w(cluster, clusters, num_tiles, dp_tiles, num_kb);
-    while (ok && w.next()) {
+    for (int tile = first_tile; tile < num_tiles && ok; tile += tile_step) {
       int pm, pn;
-      tile_coords(w.tile, num_pid_m, num_pid_n, group_m, pm, pn);
-      for (int kb = w.kb0; kb < w.kb1; ++kb, ++it) {
+      tile_coords(tile, num_pid_m, num_pid_n, group_m, pm, pn);
+      for (int kb = 0; kb < num_kb; ++kb, ++it) {
         if (!mbar_wait(smem_u32(&sh.empty[s]), ph ^ 1u, abort_flag, err, kErrWaitProducer)) {
           ok = false;
           break;
@@ -537,8 +476,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PERSISTENT ? 256 : 1
         FMT == 2 ? (make_smem_desc(smem_base + a_bytes, BK * SWB, 4 * SWB, 0) | (1ull << 61))
                  : make_smem_desc(smem_base + a_bytes, BK * SWB, 8 * SWB, SWB);
     const int ksteps = BK / KSTEP;
-    PairWork w(cluster, clusters, num_tiles, dp_tiles, num_kb);
-    for (; ok && w.next(); ++tcount) {
+    for (int tile = first_tile; tile < num_tiles && ok; tile += tile_step, ++tcount) {
       const int buf = tcount % ACC;
       const uint32_t use = static_cast<uint32_t>(tcount / ACC);
       if (PERSISTENT && !mbar_wait<true>(smem_u32(&sh.acc_empty[buf]), (use & 1u) ^ 1u,
@@ -548,7 +486,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PERSISTENT ? 256 : 1
       }
       tc_fence_after();
       const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(buf * BN);
-      for (int kb = w.kb0; kb < w.kb1; ++kb) {
+      for (int kb = 0; kb < num_kb; ++kb) {
         if (!mbar_wait(smem_u32(&sh.full[s]), ph, abort_flag, err, kErrWaitMma)) {
           ok = false;
           break;
@@ -556,7 +494,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PERSISTENT ? 256 : 1
         tc_fence_after();
         const uint32_t so4 = (static_cast<uint32_t>(s) * stage_bytes) >> 4;
         issue_kblock_any<ES, 128, SWB, 1, BN, FMT, true>(ksteps, d_tmem, adesc0 + so4,
-                                                         bdesc0 + so4, IDESC, kb == w.kb0);
+                                                         bdesc0 + so4, IDESC, kb == 0);
         mma_commit_pair(smem_u32(&sh.empty[s]));
         mma_commit_pair(peer_empty0 + static_cast<uint32_t>(s) * 8u);
         if (++s == stages) {
@@ -580,47 +518,17 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PERSISTENT ? 256 : 1
     __syncwarp();
     const int q = warp & 3;
     const uint32_t leader_acc_empty0 = mapa_shared(smem_u32(&sh.acc_empty[0]), 0);
-    // stream-K partial slots: 128 rows x BN fp32 per CTA, laid out so that
-    // each warp store / load of a float4 per lane is one 512-byte segment
-    constexpr int kSlot = 128 * BN;
-    const int fidx = 2 * cluster + static_cast<int>(rank);
     int tcount = 0;
-    PairWork w(cluster, clusters, num_tiles, dp_tiles, num_kb);
-    for (; w.next(); ++tcount) {
+    for (int tile = first_tile; tile < num_tiles; tile += tile_step, ++tcount) {
       const int buf = tcount % ACC;
       const uint32_t use = static_cast<uint32_t>(tcount / ACC);
-      bool got = mbar_wait_idle(smem_u32(&sh.acc_full[buf]), use & 1u, abort_flag, err,
-                                kErrWaitEpilogue);
-      // stream-K epilogues meet at named barriers: leave together or not at
-      // all (whole, converged warps at every barrier)
-      if constexpr (SK) {
-        __syncwarp();
-        got = named_barrier_and(1, 128, got);
-      }
-      if (!got) break;
+      if (!mbar_wait_idle(smem_u32(&sh.acc_full[buf]), use & 1u, abort_flag, err,
+                          kErrWaitEpilogue))
+        break;
       tc_fence_after();
       int pm, pn;
-      tile_coords(w.tile, num_pid_m, num_pid_n, group_m, pm, pn);
+      tile_coords(tile, num_pid_m, num_pid_n, group_m, pm, pn);
       const int row = pm * 256 + static_cast<int>(rank) * 128 + q * 32 + lane;
-      // stream-K roles of this item: hand a partial to the tile's finisher,
-      // or finish the tile with the partials of clusters [cluster+1, c_hi)
-      const bool part = SK && w.kb0 > 0;
-      const bool fin = SK && w.kb0 == 0 && w.kb1 < num_kb;
-      int c_hi = cluster + 1;
-      if constexpr (SK) {
-        if (fin) {
-          const int64_t tile_end = static_cast<int64_t>(w.tile - dp_tiles + 1) * num_kb;
-          while (c_hi < clusters && w.share_begin(c_hi) < tile_end) ++c_hi;
-          if (warp == 4 && lane == 0) {
-            for (int c2 = cluster + 1; c2 < c_hi; ++c2)
-              if (w.share_begin(c2) < w.share_begin(c2 + 1) &&
-                  !flag_wait(flags + 2 * c2 + rank, abort_flag, err, kErrWaitPartial))
-                break;
-          }
-          __syncwarp();
-          named_barrier(1, 128);
-        }
-      }
 #pragma unroll 1
       for (int c = 0; c < BN / 32; ++c) {
         uint32_t r[32];
@@ -628,33 +536,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PERSISTENT ? 256 : 1
                       static_cast<uint32_t>(buf * BN + c * 32),
                   r);
         tmem_wait_ld();
-        const int v4 = ((c * 4 + q) * 8) * 32 + lane;  // float4 index of i = 0
-        if constexpr (SK) {
-          if (part) {
-            float4* dst4 = reinterpret_cast<float4*>(ws + static_cast<int64_t>(fidx) * kSlot);
-#pragma unroll
-            for (int i = 0; i < 8; ++i)
-              __stcg(dst4 + v4 + i * 32,
-                     make_float4(__uint_as_float(r[4 * i]), __uint_as_float(r[4 * i + 1]),
-                                 __uint_as_float(r[4 * i + 2]), __uint_as_float(r[4 * i + 3])));
-            continue;
-          }
-          if (fin) {
-            for (int c2 = cluster + 1; c2 < c_hi; ++c2) {
-              if (w.share_begin(c2) == w.share_begin(c2 + 1)) continue;  // empty share
-              const float4* src4 = reinterpret_cast<const float4*>(
-                  ws + static_cast<int64_t>(2 * c2 + rank) * kSlot);
-#pragma unroll
-              for (int i = 0; i < 8; ++i) {
-                const float4 v = __ldcg(src4 + v4 + i * 32);
-                r[4 * i] = __float_as_uint(__uint_as_float(r[4 * i]) + v.x);
-                r[4 * i + 1] = __float_as_uint(__uint_as_float(r[4 * i + 1]) + v.y);
-                r[4 * i + 2] = __float_as_uint(__uint_as_float(r[4 * i + 2]) + v.z);
-                r[4 * i + 3] = __float_as_uint(__uint_as_float(r[4 * i + 3]) + v.w);
-              }
-            }
-          }
-        }
         const int col0 = pn * BN + c * 32;
         if (row < M) {
           T* dst = C + static_cast<int64_t>(row) * N + col0;
@@ -689,21 +570,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PERSISTENT ? 256 : 1
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive_cluster(leader_acc_empty0 + static_cast<uint32_t>(buf) * 8u);
-      }
-      if constexpr (SK) {
-        if (part) {
-          // every thread's partial stores are ordered before the flag
-          __threadfence();
-          named_barrier(1, 128);
-          if (warp == 4 && lane == 0) st_release_gpu(flags + fidx, 1u);
-          __syncwarp();
-        } else if (fin) {
-          // partials consumed: re-arm their flags for the next launch
-          named_barrier(1, 128);
-          if (warp == 4 && lane == 0)
-            for (int c2 = cluster + 1; c2 < c_hi; ++c2) flags[2 * c2 + rank] = 0u;
-          __syncwarp();
-        }
       }
     }
   }
@@ -791,14 +657,7 @@ gpo_status plan_matmul_tc(const gpo_key& k, Plan& p, std::string& log) {
   if (pair) {
     const uint32_t pa = 128u * BK * es, pb = static_cast<uint32_t>(BK) * (BN / 2) * es;
     const uint32_t pst = (pa + pb + 1023u) & ~1023u;
-    // Persistent pairs whose stages leave room for two CTAs per SM run
-    // stream-K with one TMEM accumulator: two clusters per SM pair split
-    // the tiles and the K blocks of the last partial wave evenly.  Deeper
-    // rings keep one CTA per SM with two accumulators.
-    const uint32_t ring = pst * static_cast<uint32_t>(k.num_stages) + 1024u;
-    const bool sk =
-        persistent && 2u * (ring + static_cast<uint32_t>(sizeof(TcShared)) + 1024u) <= 233472u;
-    const int pc = tc2_tmem_alloc((persistent && !sk ? 2 : 1) * BN);
+    const int pc = tc2_tmem_alloc((persistent ? 2 : 1) * BN);
     // Never let more CTAs share an SM than its 512 TMEM columns hold: a pair
     // allocation that had to wait on one SM of the pair while holding the
     // other could otherwise wait on a second pair doing the opposite.  The
@@ -817,7 +676,6 @@ gpo_status plan_matmul_tc(const gpo_key& k, Plan& p, std::string& log) {
     p.aux[1] = static_cast<int>(pdyn);
     p.aux[2] = persistent ? 1 : 0;
     p.aux[3] = 1;  // pair
-    p.aux[4] = sk ? 1 : 0;
     p.family = "matmul_tc";
     p.res.smem_bytes = psmem;
     p.res.tmem_cols = static_cast<uint32_t>(pc);
@@ -829,7 +687,7 @@ gpo_status plan_matmul_tc(const gpo_key& k, Plan& p, std::string& log) {
     p.res.launches_per_call = 1;
     const char* tn = k.dtype == GPO_BFLOAT16 ? "bf16" : k.dtype == GPO_FLOAT16 ? "f16" : "tf32";
     snprintf(p.res.kernel, sizeof(p.res.kernel), "matmul_tc2_kernel<%s,256,%d,cta_pair%s>", tn,
-             BN, sk ? "_streamk" : persistent ? "_persistent" : "");
+             BN, persistent ? "_persistent" : "");
     return GPO_OK;
   }
   p.aux[3] = 0;
@@ -894,7 +752,7 @@ static gpo_status run_tc(const gpo_key& k, const Plan& p, const gpo_args& a, con
   return launch_status();
 }
 
-template <typename T, int FMT, int BN, bool P, bool SK = false>
+template <typename T, int FMT, int BN, bool P>
 static gpo_status run_tc2(const gpo_key& k, const Plan& p, const gpo_args& a, const LaunchCtx& c,
                           CUtensorMapDataType dt) {
   const int es = sizeof(T);
@@ -906,36 +764,18 @@ static gpo_status run_tc2(const gpo_key& k, const Plan& p, const gpo_args& a, co
   if (!encode_2d(&ma, dt, a.in[0], M, K, es, swa / es, 128, swa)) return GPO_LAUNCH_ERROR;
   if (!encode_2d(&mb, dt, a.in[1], K, N, es, SWB / es, k.block_k, SWB, FMT == 2))
     return GPO_LAUNCH_ERROR;
-  auto kern = matmul_tc2_kernel<T, FMT, BN, P, SK>;
+  auto kern = matmul_tc2_kernel<T, FMT, BN, P>;
   const uint32_t dyn = static_cast<uint32_t>(p.aux[1]);
   gpo_status s = ensure_smem_attr(reinterpret_cast<const void*>(kern), dyn);
   if (s != GPO_OK) return s;
   const int64_t tiles = cdiv(M, 256) * cdiv(N, BN);
   const int threads = P ? 256 : 128;
-  // stream-K: every co-resident cluster takes part, however few the tiles
-  const unsigned clusters =
-      P ? persistent_clusters(reinterpret_cast<const void*>(kern), threads, dyn,
-                              SK ? INT64_MAX : tiles)
-        : static_cast<unsigned>(tiles);
-  int64_t dp = tiles;
-  float* ws = nullptr;
-  unsigned int* flags = nullptr;
-  if (SK) {
-    // split the last partial wave only when each cluster's share of it is
-    // at least 4 K blocks; finer shares cost more in partials than they save
-    const int64_t kb = cdiv(K, k.block_k);
-    const int64_t rest = tiles % clusters;
-    if (rest != 0 && rest * kb >= 4 * static_cast<int64_t>(clusters)) {
-      dp = tiles - rest;
-      s = sk_workspace(c, static_cast<size_t>(clusters) * 2u * 128u * BN * sizeof(float),
-                       2u * clusters, &ws, &flags);
-      if (s != GPO_OK) return s;
-    }
-  }
-  kern<<<2u * clusters, threads, dyn, c.stream>>>(
-      ma, mb, static_cast<T*>(a.out), static_cast<int>(M), static_cast<int>(N),
-      static_cast<int>(K), k.block_k, k.num_stages, k.group_m, swa, c.err, ws, flags,
-      static_cast<int>(dp));
+  const unsigned grid =
+      2u * (P ? persistent_clusters(reinterpret_cast<const void*>(kern), threads, dyn, tiles)
+              : static_cast<unsigned>(tiles));
+  kern<<<grid, threads, dyn, c.stream>>>(ma, mb, static_cast<T*>(a.out), static_cast<int>(M),
+                                     static_cast<int>(N), static_cast<int>(K), k.block_k,
+                                     k.num_stages, k.group_m, swa, c.err);
   return launch_status();
 }
 
@@ -943,15 +783,6 @@ template <typename T, int FMT>
 static gpo_status run_tc2_bn(const gpo_key& k, const Plan& p, const gpo_args& a,
                              const LaunchCtx& c, CUtensorMapDataType dt) {
   const bool P = p.aux[2] != 0;
-  if (p.aux[4]) {
-    switch (k.block_n) {
-      case 32: return run_tc2<T, FMT, 32, true, true>(k, p, a, c, dt);
-      case 64: return run_tc2<T, FMT, 64, true, true>(k, p, a, c, dt);
-      case 128: return run_tc2<T, FMT, 128, true, true>(k, p, a, c, dt);
-      case 256: return run_tc2<T, FMT, 256, true, true>(k, p, a, c, dt);
-      default: return GPO_INTERNAL;
-    }
-  }
   switch (k.block_n) {
     case 32: return P ? run_tc2<T, FMT, 32, true>(k, p, a, c, dt)
                       : run_tc2<T, FMT, 32, false>(k, p, a, c, dt);

@@ -65,15 +65,6 @@ def test_block_m_64_uses_m64_tensor_core_mmas_for_16_bit_inputs():
     assert rt["kernel"].startswith("matmul_simt")
 
 
-def test_persistent_pairs_with_two_ctas_per_sm_run_stream_k():
-    sk = mm({"BLOCK_M": 256, "BLOCK_N": 256, "num_stages": 3, "GROUP_M": 16}).resources()
-    assert sk["kernel"] == "matmul_tc2_kernel<bf16,256,256,cta_pair_streamk>"
-    assert sk["tmem_cols"] == 256 and 2 * sk["smem_bytes"] <= 228 * 1024
-    deep = mm({"BLOCK_M": 256, "BLOCK_N": 256, "num_stages": 6}).resources()
-    assert deep["kernel"] == "matmul_tc2_kernel<bf16,256,256,cta_pair_persistent>"
-    assert deep["tmem_cols"] == 512
-
-
 def test_shared_memory_overflow_is_a_compile_error():
     with pytest.raises(KernelBuildError) as ei:
         mm({"BLOCK_M": 256, "BLOCK_N": 256, "BLOCK_K": 128, "num_stages": 6})

@@ -53,7 +53,7 @@ MM_TC = [  # tcgen05 family: (BM, BN, BK, GROUP_M, warps, stages)
     # CTA pairs (cta_group::2); 8 warps -> persistent pairs
     (256, 256, 64, 8, 4, 3), (256, 128, 64, 4, 4, 3), (256, 32, 32, 1, 4, 2),
     (256, 256, 128, 8, 4, 2), (256, 256, 64, 8, 8, 6), (256, 128, 64, 16, 8, 8),
-    (256, 64, 64, 1, 8, 4),  # 8 warps, two CTAs per SM: stream-K persistent pairs
+    (256, 64, 64, 1, 8, 4),
     # BLOCK_M 64: M=64 MMAs (16-bit inputs; tf32 runs these on CUDA cores)
     (64, 128, 64, 8, 4, 4), (64, 256, 64, 8, 8, 4), (64, 64, 32, 1, 4, 3),
     (64, 32, 128, 4, 8, 2),
@@ -173,34 +173,6 @@ def test_tcgen05_matmul_ragged_shapes(shape, dtype):
         assert kc.launch["kernel"].startswith(want), kc.launch["kernel"]
         emu = O.emulate("matmul", shape, cfg, inputs)
         assert_close("matmul", dtype, out, emu, f"{shape} {cfg}")
-
-
-SK_CFGS = [(256, 256, 64, 16, 8, 3), (256, 128, 64, 8, 8, 4), (256, 64, 64, 1, 8, 4)]
-# shapes whose last partial wave is split: tiles % clusters != 0 with a few
-# K blocks per cluster, ragged M / N / K, shares spanning two or three
-# clusters per tile and (fewer tiles than clusters) no data-parallel tiles
-SK_SHAPES = [(2000, 4000, 1000), (3000, 2100, 2000), (4096, 4096, 1536)]
-
-
-@pytest.mark.parametrize("dtype", ["bfloat16", "float16"])
-@pytest.mark.parametrize("shape", SK_SHAPES, ids=str)
-def test_streamk_pair_matmul(shape, dtype):
-    """Stream-K persistent pairs: oracle parity, and a second launch equal
-    bit for bit to the first (the partial-tile flags re-arm every launch)."""
-    inputs = O.make_inputs("matmul", shape, dtype, 0)
-    emu = None
-    for t in SK_CFGS:
-        cfg = mm_cfg(t, dtype)
-        dev = [x.cuda() for x in inputs]
-        kc = build_callable("matmul", shape, cfg, tuple(dev))
-        assert "streamk" in kc.launch["kernel"], kc.launch["kernel"]
-        first = kc.fn().clone()
-        second = kc.fn()
-        check_device_status()
-        assert torch.equal(first, second), f"{shape} {cfg}: relaunch differs"
-        if emu is None:
-            emu = O.emulate("matmul", shape, cfg, inputs)
-        assert_close("matmul", dtype, first.cpu(), emu, f"{shape} {cfg}")
 
 
 ATT_SHAPES = [(4, 512, 64), (2, 300, 128), (1, 1000, 32), (3, 130, 128), (2, 256, 256)]
