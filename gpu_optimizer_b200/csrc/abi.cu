@@ -5,6 +5,7 @@
 #include <algorithm>
 #include <cstring>
 #include <map>
+#include <tuple>
 #include <mutex>
 #include <string>
 #include <utility>
@@ -126,11 +127,12 @@ gpo_status ensure_smem_attr(const void* func, uint32_t dyn_smem) {
 unsigned persistent_grid(const void* func, int threads, size_t dyn_smem, int sm_count,
                          int64_t work_items) {
   static std::mutex mu;
-  static std::map<std::pair<const void*, int>, int> occ;
+  // keyed by shared memory too: one kernel runs with different stage counts
+  static std::map<std::tuple<const void*, int, size_t>, int> occ;
   int per_sm = 0;
   {
     std::lock_guard<std::mutex> lk(mu);
-    auto it = occ.find({func, threads});
+    auto it = occ.find({func, threads, dyn_smem});
     if (it != occ.end()) per_sm = it->second;
   }
   if (per_sm == 0) {
@@ -141,7 +143,7 @@ unsigned persistent_grid(const void* func, int threads, size_t dyn_smem, int sm_
       per_sm = 1;
     }
     std::lock_guard<std::mutex> lk(mu);
-    occ[{func, threads}] = per_sm;
+    occ[{func, threads, dyn_smem}] = per_sm;
   }
   const int64_t g = static_cast<int64_t>(per_sm) * (sm_count > 0 ? sm_count : 148);
   return static_cast<unsigned>(std::max<int64_t>(1, std::min<int64_t>(g, work_items)));
@@ -149,11 +151,11 @@ unsigned persistent_grid(const void* func, int threads, size_t dyn_smem, int sm_
 
 unsigned persistent_clusters(const void* func, int threads, size_t dyn_smem, int64_t work_items) {
   static std::mutex mu;
-  static std::map<std::pair<const void*, int>, int> occ;
+  static std::map<std::tuple<const void*, int, size_t>, int> occ;
   int clusters = 0;
   {
     std::lock_guard<std::mutex> lk(mu);
-    auto it = occ.find({func, threads});
+    auto it = occ.find({func, threads, dyn_smem});
     if (it != occ.end()) clusters = it->second;
   }
   if (clusters == 0) {
@@ -166,7 +168,7 @@ unsigned persistent_clusters(const void* func, int threads, size_t dyn_smem, int
       clusters = 1;
     }
     std::lock_guard<std::mutex> lk(mu);
-    occ[{func, threads}] = clusters;
+    occ[{func, threads, dyn_smem}] = clusters;
   }
   return static_cast<unsigned>(std::max<int64_t>(1, std::min<int64_t>(clusters, work_items)));
 }
