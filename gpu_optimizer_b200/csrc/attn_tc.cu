@@ -35,7 +35,10 @@
 //           of 256); until then P <= 256, which 16-bit P and the fp32
 //           accumulator represent exactly as well as P <= 1.
 // TMEM columns: O [0, D), S/P buffers [D + b*BN, D + (b+1)*BN) for b < NB;
-// NB = 3 when D + 3*BN <= 512, else 2.
+// NB = 3 when D + 3*BN <= 512, else 2 -- except that with one softmax
+// warpgroup, when that layout needs more than 256 columns but two buffers
+// fit in 256 and shared memory holds two CTAs, NB = 2 and two CTAs share
+// each SM.
 #include <algorithm>
 
 #include "gpo_common.cuh"
@@ -49,6 +52,17 @@ constexpr int kAttnMaxSBufs = 3;  // S/P buffers
 
 // S/P buffers: three when TMEM has room, else two.
 __host__ __device__ constexpr int attn_sbufs(int d, int bn) { return d + 3 * bn <= 512 ? 3 : 2; }
+
+// Two S/P buffers when they fit the CTA's TMEM in half of the SM's 512
+// columns and the default layout does not (else 0): two CTAs per SM then
+// interleave their MMAs and softmax (the plan takes this when shared memory
+// also holds two CTAs).  Measured at B*H = 128, S = 4096, D = 128, BLOCK_N
+// 64: 744 vs 572 TFLOP/s (full), 653 vs 520 (causal).  One buffer (S_j,
+// softmax_j and PV_j in series within the CTA, BLOCK_N 128) measured 597 vs
+// 927 for three buffers on one CTA per SM, so it is not offered.
+__host__ __device__ constexpr int attn_duo_nb(int d, int bn) {
+  return d + attn_sbufs(d, bn) * bn > 256 && d + 2 * bn <= 256 ? 2 : 0;
+}
 
 struct AttnShared {
   uint64_t q_full;
@@ -94,8 +108,9 @@ __device__ __forceinline__ void tmem_st_cols(uint32_t taddr, const uint32_t* r) 
     tmem_st16(taddr, r);
 }
 
-template <typename T, int FMT, int BN, int D, bool CAUSAL, int WG, bool PAIR>
-__global__ void __launch_bounds__(128 + 128 * WG, 1)
+template <typename T, int FMT, int BN, int D, bool CAUSAL, int WG, bool PAIR, int NB>
+__global__ void __launch_bounds__(128 + 128 * WG,
+                                  (WG == 1 && !PAIR && attn_duo_nb(D, BN) == NB) ? 2 : 1)
     attn_tc_kernel(const __grid_constant__ CUtensorMap tma_q,
                    const __grid_constant__ CUtensorMap tma_k,
                    const __grid_constant__ CUtensorMap tma_v, T* __restrict__ O, int S,
@@ -109,7 +124,7 @@ __global__ void __launch_bounds__(128 + 128 * WG, 1)
   constexpr int SWV = (VCOLS * ES) < 128 ? (VCOLS * ES) : 128;  // swizzle of V rows
   constexpr uint32_t KV_BYTES = static_cast<uint32_t>(KROWS) * D * ES;  // = BN * VCOLS * ES
   constexpr uint32_t KV_SLOT = (KV_BYTES + 1023u) & ~1023u;
-  constexpr int NB = attn_sbufs(D, BN);
+  static_assert(NB == 2 || NB == 3, "two or three S/P buffers");
   constexpr int LAG = NB - 1;  // S MMAs run LAG blocks ahead of PV MMAs
   constexpr int COLS = D + NB * BN;
   constexpr int ALLOC = attn_tmem_alloc(COLS);
@@ -348,34 +363,33 @@ __global__ void __launch_bounds__(128 + 128 * WG, 1)
         ok = false;
       ok = __all_sync(0xffffffffu, ok);  // warp-uniform from here on
       tc_fence_after();
-      float sv[SC];
+      uint32_t sv[SC];  // S scores (fp32 bits) as the TMEM loads leave them
       float mb = 0.f;
+      // Mask padding / future keys only where the block needs it (block-
+      // uniform test on the tile's first row); work on raw scores, with the
+      // log2-domain scale folded into the exponent's FMA below.
+      const int key0 = j * BN + col0;
+      const bool need_mask = j * BN + BN > S || (CAUSAL && j * BN + BN - 1 > q0);
+      auto f = [&](int i) { return __uint_as_float(sv[i]); };
       if (ok) {
-        // all TMEM loads of this warp's columns in flight before one wait
-        uint32_t r[SC];
+        // this warp's share of S_j -> sv, all TMEM loads in flight before
+        // one wait
 #pragma unroll
         for (int c = 0; c < SC / SCH; ++c)
-          tmem_ld_cols<SCH>(sp + static_cast<uint32_t>(col0 + c * SCH), r + c * SCH);
+          tmem_ld_cols<SCH>(sp + static_cast<uint32_t>(col0 + c * SCH), sv + c * SCH);
         tmem_wait_ld();
-#pragma unroll
-        for (int i = 0; i < SC; ++i) sv[i] = __uint_as_float(r[i]);
-        // Mask padding / future keys only where the block needs it (block-
-        // uniform test on the tile's first row); work on raw scores, with
-        // the log2-domain scale folded into the exponent's FMA below.
-        const int key0 = j * BN + col0;
-        const bool need_mask = j * BN + BN > S || (CAUSAL && j * BN + BN - 1 > q0);
         if (need_mask) {
 #pragma unroll
           for (int i = 0; i < SC; ++i) {
             const int key = key0 + i;
-            if (key >= S || (CAUSAL && key > qrow)) sv[i] = -INFINITY;
+            if (key >= S || (CAUSAL && key > qrow)) sv[i] = __float_as_uint(-INFINITY);
           }
         }
         // row max: four independent three-input max chains
-        float mx[4] = {sv[0], sv[1], sv[2], sv[3]};
+        float mx[4] = {f(0), f(1), f(2), f(3)};
 #pragma unroll
         for (int i = 4; i + 1 < SC; i += 2)
-          mx[(i >> 1) & 3] = fmax3(mx[(i >> 1) & 3], sv[i], sv[i + 1]);
+          mx[(i >> 1) & 3] = fmax3(mx[(i >> 1) & 3], f(i), f(i + 1));
         mb = fmaxf(fmax3(mx[0], mx[1], mx[2]), mx[3]) * scale_log2;
       }
       if constexpr (WG == 2) {
@@ -425,24 +439,26 @@ __global__ void __launch_bounds__(128 + 128 * WG, 1)
       const float2 shift2 = make_float2(neg_m, neg_m);
       float2 rs[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f),
                       make_float2(0.f, 0.f)};
-      uint32_t pk[SC / 2];
+      // P_j -> TMEM over the first BN/2 columns of its own S buffer (this
+      // warp: columns [col0/2, col0/2 + SC/2)), 16 columns as soon as they
+      // are packed.  The MMA issuer writes S_{j+NB} into this buffer only
+      // after issuing PV_j, and tcgen05 MMAs execute in issue order.
 #pragma unroll
-      for (int g = 0; g < SC / 2; ++g) {
-        const float2 x = __ffma2_rn(make_float2(sv[2 * g], sv[2 * g + 1]), scale2, shift2);
-        const float2 p = make_float2(ex2_approx(x.x), ex2_approx(x.y));  // -inf -> 0
-        rs[g & 3] = __fadd2_rn(rs[g & 3], p);
-        pk[g] = FMT == 1 ? pack_bf16(p.x, p.y) : pack_f16(p.x, p.y);
+      for (int c = 0; c < (SC / 2) / 16; ++c) {
+        uint32_t pk[16];
+#pragma unroll
+        for (int g2 = 0; g2 < 16; ++g2) {
+          const int g = c * 16 + g2;
+          const float2 x = __ffma2_rn(make_float2(f(2 * g), f(2 * g + 1)), scale2, shift2);
+          const float2 p = make_float2(ex2_approx(x.x), ex2_approx(x.y));  // -inf -> 0
+          rs[g & 3] = __fadd2_rn(rs[g & 3], p);
+          pk[g2] = FMT == 1 ? pack_bf16(p.x, p.y) : pack_f16(p.x, p.y);
+        }
+        tmem_st16(sp + static_cast<uint32_t>(col0 / 2 + c * 16), pk);
       }
       const float2 rs01 = __fadd2_rn(rs[0], rs[1]), rs23 = __fadd2_rn(rs[2], rs[3]);
       const float2 rsum = __fadd2_rn(rs01, rs23);
       l += rsum.x + rsum.y;
-      // P_j -> TMEM over the first BN/2 columns of its own S buffer (this
-      // warp: columns [col0/2, col0/2 + SC/2)).  The MMA issuer writes
-      // S_{j+NB} into this buffer only after issuing PV_j, and tcgen05 MMAs
-      // execute in issue order.
-#pragma unroll
-      for (int c = 0; c < (SC / 2) / 16; ++c)
-        tmem_st16(sp + static_cast<uint32_t>(col0 / 2 + c * 16), pk + c * 16);
       tmem_wait_st();
       tc_fence_before();
       __syncwarp();
@@ -559,10 +575,15 @@ gpo_status plan_attention_tc(const gpo_key& k, Plan& p, std::string& log) {
           " + 2 S buffers x " + std::to_string(BN) + ") > 512";
     return GPO_COMPILE_ERROR;
   }
-  const int cols_needed = D + attn_sbufs(D, BN) * BN;
   const uint32_t dyn =
       attn_tc_smem(BN, D, k.num_stages, pair) + (wg == 2 ? kAttnXchgBytes : 0u);
   const uint32_t smem = dyn + static_cast<uint32_t>(sizeof(AttnShared));
+  // two CTAs per SM when two S/P buffers fit TMEM's half and shared memory
+  // holds two CTAs (228 KB per SM, 1 KB reserved per CTA)
+  const bool duo =
+      !pair && wg == 1 && attn_duo_nb(D, BN) > 0 && 2u * (smem + 1024u) <= 233472u;
+  const int nb = duo ? attn_duo_nb(D, BN) : attn_sbufs(D, BN);
+  const int cols_needed = D + nb * BN;
   if (smem > kMaxSmemPerCta) {
     log = "shared memory " + std::to_string(smem) + " B (Q tile + " +
           std::to_string(k.num_stages) + " K and V stages) exceeds the 232448 B per-CTA limit";
@@ -571,6 +592,7 @@ gpo_status plan_attention_tc(const gpo_key& k, Plan& p, std::string& log) {
   p.aux[0] = static_cast<int>(dyn);
   p.aux[1] = wg;
   p.aux[2] = pair ? 1 : 0;
+  p.aux[3] = nb;
   p.family = "attn_tc";
   p.res.smem_bytes = smem;
   p.res.tmem_cols = static_cast<uint32_t>(attn_tmem_alloc(cols_needed));
@@ -581,12 +603,12 @@ gpo_status plan_attention_tc(const gpo_key& k, Plan& p, std::string& log) {
   p.res.launches_per_call = 1;
   snprintf(p.res.kernel, sizeof(p.res.kernel), "attn_tc_kernel<%s,BN=%d,D=%d,%s,wg=%d,sbufs=%d%s>",
            k.dtype == GPO_BFLOAT16 ? "bf16" : "f16", BN, D,
-           k.task == GPO_TASK_ATTENTION_CAUSAL ? "causal" : "full", wg, attn_sbufs(D, BN),
+           k.task == GPO_TASK_ATTENTION_CAUSAL ? "causal" : "full", wg, nb,
            pair ? ",cta_pair" : "");
   return GPO_OK;
 }
 
-template <typename T, int FMT, int BN, int D, bool CAUSAL, int WG, bool PAIR>
+template <typename T, int FMT, int BN, int D, bool CAUSAL, int WG, bool PAIR, int NB>
 static gpo_status run_attn_tc_wg(const gpo_key& k, const Plan& p, const gpo_args& a,
                                  const LaunchCtx& c, CUtensorMapDataType dt) {
   const uint64_t BH = static_cast<uint64_t>(k.shape[0]), S = static_cast<uint64_t>(k.shape[1]);
@@ -597,7 +619,7 @@ static gpo_status run_attn_tc_wg(const gpo_key& k, const Plan& p, const gpo_args
       !encode_bsd(&mk, dt, a.in[1], BH, S, D, PAIR ? BN / 2 : BN, SW) ||
       !encode_bsd(&mv, dt, a.in[2], BH, S, D, BN, SWV))
     return GPO_LAUNCH_ERROR;
-  auto kern = attn_tc_kernel<T, FMT, BN, D, CAUSAL, WG, PAIR>;
+  auto kern = attn_tc_kernel<T, FMT, BN, D, CAUSAL, WG, PAIR, NB>;
   const uint32_t dyn = static_cast<uint32_t>(p.aux[0]);
   gpo_status s = ensure_smem_attr(reinterpret_cast<const void*>(kern), dyn);
   if (s != GPO_OK) return s;
@@ -633,15 +655,24 @@ template <typename T, int FMT, int BN, int D, bool CAUSAL>
 static gpo_status run_attn_tc(const gpo_key& k, const Plan& p, const gpo_args& a,
                               const LaunchCtx& c, CUtensorMapDataType dt) {
   if constexpr (D + 2 * BN <= 512) {
+    constexpr int NB = attn_sbufs(D, BN);
     const bool pair = p.aux[2] != 0;
+    constexpr int NBD = attn_duo_nb(D, BN);
+    if constexpr (NBD > 0) {
+      if (p.aux[3] == NBD) {
+        if (pair || p.aux[1] != 1) return GPO_INTERNAL;
+        return run_attn_tc_wg<T, FMT, BN, D, CAUSAL, 1, false, NBD>(k, p, a, c, dt);
+      }
+    }
+    if (p.aux[3] != NB) return GPO_INTERNAL;
     if constexpr (BN >= 64) {
       if (p.aux[1] == 2)
-        return pair ? run_attn_tc_wg<T, FMT, BN, D, CAUSAL, 2, true>(k, p, a, c, dt)
-                    : run_attn_tc_wg<T, FMT, BN, D, CAUSAL, 2, false>(k, p, a, c, dt);
+        return pair ? run_attn_tc_wg<T, FMT, BN, D, CAUSAL, 2, true, NB>(k, p, a, c, dt)
+                    : run_attn_tc_wg<T, FMT, BN, D, CAUSAL, 2, false, NB>(k, p, a, c, dt);
     }
     if (p.aux[1] != 1) return GPO_INTERNAL;
-    return pair ? run_attn_tc_wg<T, FMT, BN, D, CAUSAL, 1, true>(k, p, a, c, dt)
-                : run_attn_tc_wg<T, FMT, BN, D, CAUSAL, 1, false>(k, p, a, c, dt);
+    return pair ? run_attn_tc_wg<T, FMT, BN, D, CAUSAL, 1, true, NB>(k, p, a, c, dt)
+                : run_attn_tc_wg<T, FMT, BN, D, CAUSAL, 1, false, NB>(k, p, a, c, dt);
   } else {
     return GPO_INTERNAL;  // rejected by the plan (TMEM)
   }

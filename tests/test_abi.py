@@ -102,6 +102,15 @@ def test_attention_plans():
                         {**base, "BLOCK_M": 256, "num_stages": 4}).resources()
     assert r5["kernel"].endswith("sbufs=3,cta_pair>") and r5["grid"] == [32, 128, 1]
     assert r5["threads_per_cta"] == 256 and r5["tmem_cols"] == 512
+    # BLOCK_N 64 (D 128), one warpgroup, two stages: two S/P buffers keep the
+    # CTA within 256 TMEM columns so that two CTAs share an SM
+    r6 = compile_module("attention", (128, 4096, 128), {**base, "BLOCK_N": 64}).resources()
+    assert r6["kernel"].endswith("wg=1,sbufs=2>") and r6["tmem_cols"] == 256
+    assert 2 * (r6["smem_bytes"] + 1024) <= 228 * 1024
+    # three stages no longer leave room for two CTAs: three buffers, 512 columns
+    r7 = compile_module("attention", (128, 4096, 128),
+                        {**base, "BLOCK_N": 64, "num_stages": 3}).resources()
+    assert r7["kernel"].endswith("sbufs=3>") and r7["tmem_cols"] == 512
     # D = 256 with BLOCK_N 128: O 256 + 2 S buffers x 128 fill TMEM (two buffers)
     r4 = compile_module("attention", (4, 512, 256), {**base, "num_stages": 1}).resources()
     assert r4["kernel"].endswith("sbufs=2>") and r4["tmem_cols"] == 512
