@@ -98,7 +98,8 @@ def task_configs(name, dtype):
         if dtype != "float32":
             cfgs += [{"BLOCK_M": 128, "BLOCK_N": bn, "num_warps": w, "num_stages": s,
                       "dtype": dtype} for bn, s, w in ((32, 1, 4), (64, 2, 4), (128, 2, 4),
-                                                       (32, 4, 4), (64, 2, 8), (32, 3, 8))]
+                                                       (32, 4, 4), (64, 2, 8), (32, 3, 8),
+                                                       (128, 2, 8))]
         return cfgs
     raise KeyError(name)
 
