@@ -194,8 +194,9 @@ gpo_status launch_attention_simt(const gpo_key& k, const Plan& p, const gpo_args
 }
 
 // ------------------------------------------------------------- dispatcher
-// Tensor cores for 16-bit inputs with BLOCK_M = 128 (one CTA per query
-// tile) or 256 (a CTA pair on two query tiles), BLOCK_N in {32, 64, 128},
+// Tensor cores for 16-bit inputs with BLOCK_M = 64 (64-row query tiles,
+// M=64 MMAs), 128 (one CTA per query tile) or 256 (a CTA pair on two query
+// tiles), BLOCK_N in {32, 64, 128},
 // head dim in {32, 64, 128, 256} and num_warps 4 (one softmax warpgroup) or
 // 8 (two); CUDA cores otherwise.  aux[7] records the choice (1 = tcgen05).
 gpo_status plan_attention(const gpo_key& k, Plan& p, std::string& log) {
@@ -210,7 +211,7 @@ gpo_status plan_attention(const gpo_key& k, Plan& p, std::string& log) {
     return GPO_BAD_CONFIG;
   }
   const bool tc = (k.dtype == GPO_BFLOAT16 || k.dtype == GPO_FLOAT16) &&
-                  (k.block_m == 128 || k.block_m == 256) &&
+                  (k.block_m == 64 || k.block_m == 128 || k.block_m == 256) &&
                   (k.block_n == 32 || k.block_n == 64 || k.block_n == 128) && D >= 32 &&
                   D <= 256 && (k.num_warps == 4 || k.num_warps == 8);
   if (tc) {

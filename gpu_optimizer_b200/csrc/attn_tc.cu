@@ -2,8 +2,9 @@
 // causal.
 //
 // Replaces attention_kernel (compiler/triton/kernels.py:212-270) for 16-bit
-// inputs with BLOCK_M = 128.  One CTA per (128-row query tile, batch*head);
-// causal grids visit the longest query tiles first.
+// inputs with BLOCK_M = 64, 128 or 256.  One CTA per (128-row query tile,
+// batch*head) -- 64-row tiles with M=64 MMAs for BLOCK_M 64, a CTA pair on
+// two tiles for 256; causal grids visit the longest query tiles first.
 //
 // Warp roles:
 //   warp 0  TMA producer of Q (once) and of the K ring (num_stages slots).
@@ -108,7 +109,7 @@ __device__ __forceinline__ void tmem_st_cols(uint32_t taddr, const uint32_t* r) 
     tmem_st16(taddr, r);
 }
 
-template <typename T, int FMT, int BN, int D, bool CAUSAL, int WG, bool PAIR, int NB>
+template <typename T, int FMT, int BN, int D, bool CAUSAL, int WG, bool PAIR, int NB, int TM>
 __global__ void __launch_bounds__(128 + 128 * WG,
                                   (WG == 1 && !PAIR && attn_duo_nb(D, BN) == NB) ? 2 : 1)
     attn_tc_kernel(const __grid_constant__ CUtensorMap tma_q,
@@ -117,7 +118,11 @@ __global__ void __launch_bounds__(128 + 128 * WG,
                    int stages, float scale_log2, unsigned int* err) {
   constexpr int ES = 2;
   constexpr int SWQ = (D * ES) < 128 ? (D * ES) : 128;  // swizzle of Q/K/V rows
-  constexpr uint32_t Q_BYTES = 128u * D * ES;
+  // TM: query rows per CTA (128, or 64 with M=64 MMAs: D / S row 16g + r
+  // sits in TMEM lane 32g + r, and an M=64 MMA reads its A operand (P) from
+  // the same lanes)
+  static_assert(TM == 128 || (TM == 64 && WG == 1 && !PAIR), "64-row tiles: one warpgroup");
+  constexpr uint32_t Q_BYTES = static_cast<uint32_t>(TM) * D * ES;
   // PAIR: each CTA stages half of K's rows and half of V's columns
   constexpr int KROWS = PAIR ? BN / 2 : BN;     // K rows per CTA
   constexpr int VCOLS = PAIR ? D / 2 : D;       // V columns per CTA
@@ -128,7 +133,7 @@ __global__ void __launch_bounds__(128 + 128 * WG,
   constexpr int LAG = NB - 1;  // S MMAs run LAG blocks ahead of PV MMAs
   constexpr int COLS = D + NB * BN;
   constexpr int ALLOC = attn_tmem_alloc(COLS);
-  constexpr int MMA_M = PAIR ? 256 : 128;
+  constexpr int MMA_M = PAIR ? 256 : TM;
   constexpr uint32_t IDESC_S = make_idesc(FMT, MMA_M, BN, false, false);
   constexpr uint32_t IDESC_O = make_idesc(FMT, MMA_M, D, false, true);
   constexpr int SC = BN / WG;        // S columns per softmax warp
@@ -150,15 +155,15 @@ __global__ void __launch_bounds__(128 + 128 * WG,
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   // PAIR: cluster c holds query tiles 2c (even CTA) and 2c + 1 (odd CTA)
   const uint32_t rank = PAIR ? cluster_ctarank() : 0u;
-  const int units = PAIR ? (S + 255) / 256 : (S + 127) / 128;  // tiles or tile pairs
+  const int units = PAIR ? (S + 255) / 256 : (S + TM - 1) / TM;  // tiles or tile pairs
   const int unit = static_cast<int>(PAIR ? (blockIdx.x >> 1) : blockIdx.x);
   // longest causal rows first; identity order for the non-causal task
   const int ut = CAUSAL ? (units - 1 - unit) : unit;
-  const int q0 = PAIR ? (2 * ut + static_cast<int>(rank)) * 128 : ut * 128;
+  const int q0 = PAIR ? (2 * ut + static_cast<int>(rank)) * 128 : ut * TM;
   const int bh = blockIdx.y;
   // K/V blocks the MMAs run over (causal: up to the diagonal of the unit's
   // last tile; the even CTA of a pair masks its extra blocks to P = 0)
-  const int kv_len = CAUSAL ? min(S, (PAIR ? 2 * ut + 2 : ut + 1) * 128) : S;
+  const int kv_len = CAUSAL ? min(S, PAIR ? (2 * ut + 2) * 128 : (ut + 1) * TM) : S;
   const int nblk = (kv_len + BN - 1) / BN;
 
   if (threadIdx.x == 0) {
@@ -223,7 +228,7 @@ __global__ void __launch_bounds__(128 + 128 * WG,
       if (rank == 0) mbar_arrive_expect_tx(smem_u32(&sh.q_full), mult * Q_BYTES);
 #pragma unroll
       for (int a = 0; a < (D * ES) / SWQ; ++a)
-        load(q_smem + a * 128 * SWQ, &tma_q, lead(&sh.q_full), a * (SWQ / ES), q0);
+        load(q_smem + a * TM * SWQ, &tma_q, lead(&sh.q_full), a * (SWQ / ES), q0);
     }
     for (int j = 0; j < nblk; ++j) {
       const int s = j % stages;
@@ -315,7 +320,7 @@ __global__ void __launch_bounds__(128 + 128 * WG,
 #pragma unroll
       for (int kk = 0; kk < D / 16; ++kk) {
         const uint32_t kbyte = static_cast<uint32_t>(kk) * 32u;
-        const uint32_t aoff = (kbyte / SWQ) * (128 * SWQ) + (kbyte % SWQ);
+        const uint32_t aoff = (kbyte / SWQ) * (TM * SWQ) + (kbyte % SWQ);
         const uint32_t boff = (kbyte / SWQ) * (KROWS * SWQ) + (kbyte % SWQ);
         const uint64_t adesc = make_smem_desc(q_smem + aoff, 16, 8 * SWQ, SWQ);
         const uint64_t bdesc = make_smem_desc(ks + boff, 16, 8 * SWQ, SWQ);
@@ -343,8 +348,12 @@ __global__ void __launch_bounds__(128 + 128 * WG,
     // ------------------------------------------- softmax / correction / epilogue
     const int wg = (warp - 4) >> 2;  // warpgroup: which half of the columns
     const int q = warp & 3;          // TMEM lane quarter of this warp
-    const int row = q * 32 + lane;   // query row within the tile == TMEM lane
-    const int qrow = q0 + row;
+    // query row within the tile: TMEM lane 32q + lane (TM = 64: lanes
+    // 32q + [0, 16) hold rows 16q + lane; the other lanes carry no row and
+    // mask their whole S row, so their P is 0 and they store nothing)
+    const int row = TM == 128 ? q * 32 + lane : q * 16 + lane;
+    const bool active = TM == 128 || lane < 16;
+    const int qrow = active ? q0 + row : S;
     const uint32_t lane_addr = static_cast<uint32_t>(q * 32) << 16;
     const uint32_t o_tmem = tmem + lane_addr + static_cast<uint32_t>(wg * OC);
     const int col0 = wg * SC;  // first S column of this warp
@@ -378,11 +387,11 @@ __global__ void __launch_bounds__(128 + 128 * WG,
         for (int c = 0; c < SC / SCH; ++c)
           tmem_ld_cols<SCH>(sp + static_cast<uint32_t>(col0 + c * SCH), sv + c * SCH);
         tmem_wait_ld();
-        if (need_mask) {
+        if (need_mask || !active) {
 #pragma unroll
           for (int i = 0; i < SC; ++i) {
             const int key = key0 + i;
-            if (key >= S || (CAUSAL && key > qrow)) sv[i] = __float_as_uint(-INFINITY);
+            if (!active || key >= S || (CAUSAL && key > qrow)) sv[i] = __float_as_uint(-INFINITY);
           }
         }
         // row max: four independent three-input max chains
@@ -544,16 +553,17 @@ static bool encode_bsd(CUtensorMap* map, CUtensorMapDataType dt, const void* ptr
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-static uint32_t attn_tc_smem(int BN, int D, int stages, bool pair) {
+static uint32_t attn_tc_smem(int BN, int D, int stages, bool pair, int tm) {
   auto al = [](uint32_t x) { return (x + 1023u) & ~1023u; };
-  const uint32_t q = 128u * D * 2;
+  const uint32_t q = static_cast<uint32_t>(tm) * D * 2;
   const uint32_t kv = static_cast<uint32_t>(pair ? BN / 2 : BN) * D * 2;  // a K (or V) slot
   return al(q) + static_cast<uint32_t>(stages) * 2 * al(kv) + 1024u;
 }
 
 // Plan: aux[0] = dynamic smem bytes, aux[1] = softmax warpgroups (WG),
-// aux[2] = CTA pair.
-// BLOCK_M 128 -> one 128-row query tile per CTA; 256 -> a cluster of two
+// aux[2] = CTA pair, aux[3] = S/P buffers, aux[4] = query rows per CTA.
+// BLOCK_M 64 -> one 64-row query tile per CTA (M=64 MMAs, one softmax
+// warpgroup); 128 -> one 128-row query tile per CTA; 256 -> a cluster of two
 // CTAs on two consecutive query tiles of a head, sharing each K/V block
 // through M=256 cta_group::2 MMAs (each CTA stages half of K's rows and half
 // of V's columns, halving the shared-memory and TMA bytes per tile).
@@ -563,8 +573,9 @@ static uint32_t attn_tc_smem(int BN, int D, int stages, bool pair) {
 gpo_status plan_attention_tc(const gpo_key& k, Plan& p, std::string& log) {
   const int D = static_cast<int>(k.shape[2]);
   const int BN = k.block_n;
-  const int wg = (k.num_warps == 8 && BN >= 64) ? 2 : 1;
   const bool pair = k.block_m == 256;
+  const int tm = k.block_m == 64 ? 64 : 128;  // query rows per CTA
+  const int wg = (k.num_warps == 8 && BN >= 64 && tm == 128) ? 2 : 1;
   if (k.num_stages < 1 || k.num_stages > kAttnMaxStages) {
     log = "num_stages must be in [1, 4]";
     return GPO_BAD_CONFIG;
@@ -576,7 +587,7 @@ gpo_status plan_attention_tc(const gpo_key& k, Plan& p, std::string& log) {
     return GPO_COMPILE_ERROR;
   }
   const uint32_t dyn =
-      attn_tc_smem(BN, D, k.num_stages, pair) + (wg == 2 ? kAttnXchgBytes : 0u);
+      attn_tc_smem(BN, D, k.num_stages, pair, tm) + (wg == 2 ? kAttnXchgBytes : 0u);
   const uint32_t smem = dyn + static_cast<uint32_t>(sizeof(AttnShared));
   // two CTAs per SM when two S/P buffers fit TMEM's half and shared memory
   // holds two CTAs (228 KB per SM, 1 KB reserved per CTA)
@@ -593,37 +604,39 @@ gpo_status plan_attention_tc(const gpo_key& k, Plan& p, std::string& log) {
   p.aux[1] = wg;
   p.aux[2] = pair ? 1 : 0;
   p.aux[3] = nb;
+  p.aux[4] = tm;
   p.family = "attn_tc";
   p.res.smem_bytes = smem;
   p.res.tmem_cols = static_cast<uint32_t>(attn_tmem_alloc(cols_needed));
   p.res.threads_per_cta = static_cast<uint32_t>(128 + 128 * wg);
-  p.res.grid_x = static_cast<uint32_t>(pair ? 2 * cdiv(k.shape[1], 256) : cdiv(k.shape[1], 128));
+  p.res.grid_x = static_cast<uint32_t>(pair ? 2 * cdiv(k.shape[1], 256) : cdiv(k.shape[1], tm));
   p.res.grid_y = static_cast<uint32_t>(k.shape[0]);
   p.res.grid_z = 1;
   p.res.launches_per_call = 1;
-  snprintf(p.res.kernel, sizeof(p.res.kernel), "attn_tc_kernel<%s,BN=%d,D=%d,%s,wg=%d,sbufs=%d%s>",
-           k.dtype == GPO_BFLOAT16 ? "bf16" : "f16", BN, D,
+  snprintf(p.res.kernel, sizeof(p.res.kernel), "attn_tc_kernel<%s,%sBN=%d,D=%d,%s,wg=%d,sbufs=%d%s>",
+           k.dtype == GPO_BFLOAT16 ? "bf16" : "f16", tm == 64 ? "BM=64," : "", BN, D,
            k.task == GPO_TASK_ATTENTION_CAUSAL ? "causal" : "full", wg, nb,
            pair ? ",cta_pair" : "");
   return GPO_OK;
 }
 
-template <typename T, int FMT, int BN, int D, bool CAUSAL, int WG, bool PAIR, int NB>
+template <typename T, int FMT, int BN, int D, bool CAUSAL, int WG, bool PAIR, int NB,
+          int TM = 128>
 static gpo_status run_attn_tc_wg(const gpo_key& k, const Plan& p, const gpo_args& a,
                                  const LaunchCtx& c, CUtensorMapDataType dt) {
   const uint64_t BH = static_cast<uint64_t>(k.shape[0]), S = static_cast<uint64_t>(k.shape[1]);
   constexpr int SW = (D * 2) < 128 ? (D * 2) : 128;
   constexpr int SWV = (PAIR ? D : D * 2) < 128 ? (PAIR ? D : D * 2) : 128;  // V half: D/2 columns
   CUtensorMap mq, mk, mv;
-  if (!encode_bsd(&mq, dt, a.in[0], BH, S, D, 128, SW) ||
+  if (!encode_bsd(&mq, dt, a.in[0], BH, S, D, TM, SW) ||
       !encode_bsd(&mk, dt, a.in[1], BH, S, D, PAIR ? BN / 2 : BN, SW) ||
       !encode_bsd(&mv, dt, a.in[2], BH, S, D, BN, SWV))
     return GPO_LAUNCH_ERROR;
-  auto kern = attn_tc_kernel<T, FMT, BN, D, CAUSAL, WG, PAIR, NB>;
+  auto kern = attn_tc_kernel<T, FMT, BN, D, CAUSAL, WG, PAIR, NB, TM>;
   const uint32_t dyn = static_cast<uint32_t>(p.aux[0]);
   gpo_status s = ensure_smem_attr(reinterpret_cast<const void*>(kern), dyn);
   if (s != GPO_OK) return s;
-  const dim3 grid(static_cast<unsigned>(PAIR ? 2 * cdiv(S, 256) : cdiv(S, 128)),
+  const dim3 grid(static_cast<unsigned>(PAIR ? 2 * cdiv(S, 256) : cdiv(S, TM)),
                   static_cast<unsigned>(BH));
   const float scale_log2 = 1.4426950408889634f / sqrtf(static_cast<float>(D));
   T* out = static_cast<T*>(a.out);
@@ -658,6 +671,14 @@ static gpo_status run_attn_tc(const gpo_key& k, const Plan& p, const gpo_args& a
     constexpr int NB = attn_sbufs(D, BN);
     const bool pair = p.aux[2] != 0;
     constexpr int NBD = attn_duo_nb(D, BN);
+    if (p.aux[4] == 64) {  // 64-row query tiles: one warpgroup, no pair
+      if (pair || p.aux[1] != 1) return GPO_INTERNAL;
+      if constexpr (NBD > 0) {
+        if (p.aux[3] == NBD) return run_attn_tc_wg<T, FMT, BN, D, CAUSAL, 1, false, NBD, 64>(k, p, a, c, dt);
+      }
+      if (p.aux[3] != NB) return GPO_INTERNAL;
+      return run_attn_tc_wg<T, FMT, BN, D, CAUSAL, 1, false, NB, 64>(k, p, a, c, dt);
+    }
     if constexpr (NBD > 0) {
       if (p.aux[3] == NBD) {
         if (pair || p.aux[1] != 1) return GPO_INTERNAL;

@@ -111,6 +111,11 @@ def test_attention_plans():
     r7 = compile_module("attention", (128, 4096, 128),
                         {**base, "BLOCK_N": 64, "num_stages": 3}).resources()
     assert r7["kernel"].endswith("sbufs=3>") and r7["tmem_cols"] == 512
+    # BLOCK_M 64: 64-row query tiles on M=64 MMAs, one softmax warpgroup
+    r8 = compile_module("attention_causal", (128, 4096, 128),
+                        {**base, "BLOCK_M": 64, "num_warps": 8}).resources()
+    assert r8["kernel"] == "attn_tc_kernel<bf16,BM=64,BN=128,D=128,causal,wg=1,sbufs=3>"
+    assert r8["grid"] == [64, 128, 1] and r8["threads_per_cta"] == 256
     # D = 256 with BLOCK_N 128: O 256 + 2 S buffers x 128 fill TMEM (two buffers)
     r4 = compile_module("attention", (4, 512, 256), {**base, "num_stages": 1}).resources()
     assert r4["kernel"].endswith("sbufs=2>") and r4["tmem_cols"] == 512

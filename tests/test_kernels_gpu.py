@@ -188,8 +188,9 @@ def test_tcgen05_attention_shapes(shape, dtype, causal):
     ref = O.reference(name, inputs)
     ran = 0
     # BLOCK_M 256: CTA pairs on two query tiles (odd tile counts leave the
-    # last pair's second tile partly or wholly past S)
-    for bm, bn, stages, warps in [(bm, bn, st, w) for bm in (128, 256) for bn in (32, 64, 128)
+    # last pair's second tile partly or wholly past S); BLOCK_M 64: 64-row
+    # tiles on M=64 MMAs
+    for bm, bn, stages, warps in [(bm, bn, st, w) for bm in (64, 128, 256) for bn in (32, 64, 128)
                                   for st in (1, 2, 3) for w in (4, 8)]:
         if True:
             cfg = {"BLOCK_M": bm, "BLOCK_N": bn, "num_warps": warps, "num_stages": stages,
@@ -202,7 +203,7 @@ def test_tcgen05_attention_shapes(shape, dtype, causal):
             assert kc.launch["kernel"].startswith("attn_tc_kernel")
             assert_close(name, dtype, out, ref, f"{shape} {cfg}")
             ran += 1
-    assert ran >= 6
+    assert ran >= 9
 
 
 def test_edge_cases():
