@@ -463,9 +463,9 @@ gpo_status launch_matmul_simt(const gpo_key& k, const Plan& p, const gpo_args& a
 }
 
 // ------------------------------------------------------------- dispatcher
-// Tensor cores for 16-bit / tf32 with BLOCK_M in {128, 256} (16-bit also
-// 64) and BLOCK_N in {32..256} when TMA can describe the operands; CUDA
-// cores otherwise.
+// Tensor cores for 16-bit / tf32 with BLOCK_M in {64, 128, 256} and
+// BLOCK_N in {32..256} when TMA can describe the operands; CUDA cores
+// otherwise.
 // aux[7] records the choice (1 = tcgen05).
 gpo_status plan_matmul(const gpo_key& k, Plan& p, std::string& log) {
   if (k.ndim != 3 || k.shape[0] < 0 || k.shape[1] < 0 || k.shape[2] < 0) {
@@ -474,8 +474,7 @@ gpo_status plan_matmul(const gpo_key& k, Plan& p, std::string& log) {
   }
   const int es = dtype_bytes(k.dtype);
   const bool tc_dtype = k.dtype != GPO_FLOAT32;
-  const bool tc_tile = (k.block_m == 128 || k.block_m == 256 ||
-                        (k.block_m == 64 && k.dtype != GPO_TF32)) &&
+  const bool tc_tile = (k.block_m == 64 || k.block_m == 128 || k.block_m == 256) &&
                        k.block_n >= 32 && k.block_k * es >= 32 &&
                        (k.num_warps == 4 || k.num_warps == 8);
   const bool tc_shape = (k.shape[2] * es) % 16 == 0 && (k.shape[1] * es) % 16 == 0;

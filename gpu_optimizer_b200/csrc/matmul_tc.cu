@@ -1,14 +1,13 @@
 // C = A @ B on the 5th-generation tensor cores (tcgen05) for sm_100a.
 //
 // Replaces matmul_kernel (compiler/triton/kernels.py:26-65) for 16-bit and
-// tf32 candidates whose BLOCK_M is 128 or 256 (and 16-bit ones with
-// BLOCK_M 64).  A is M x K row-major
+// tf32 candidates whose BLOCK_M is 64, 128 or 256.  A is M x K row-major
 // (K-major operand), B is K x N row-major (MN-major operand, the layout the
 // reference passes: runner.py:107 stride_bk = N), C is M x N in A's dtype
 // (runner.py:101), fp32 accumulation in TMEM.
 //
 // Config mapping (one instantiation per (dtype, BLOCK_M, BLOCK_N, warps)):
-//   BLOCK_M    : 64  -> one M=64 MMA per K step (16-bit only); D row
+//   BLOCK_M    : 64  -> one M=64 MMA per K step; D row
 //                16g + r sits in TMEM lane 32g + r (g < 4, r < 16), so each
 //                epilogue warp stores 16 rows.
 //                128 -> one M=128 MMA per K step (matmul_tc_kernel).
@@ -619,8 +618,8 @@ gpo_status plan_matmul_tc(const gpo_key& k, Plan& p, std::string& log) {
   const int es = dtype_bytes(k.dtype);
   const int BM = k.block_m, BN = k.block_n, BK = k.block_k;
   const int64_t M = k.shape[0], N = k.shape[1], K = k.shape[2];
-  if ((BM != 64 || k.dtype == GPO_TF32) && BM != 128 && BM != 256) {
-    log = "tcgen05 family needs BLOCK_M 128 or 256 (or 64 for 16-bit inputs)";
+  if (BM != 64 && BM != 128 && BM != 256) {
+    log = "tcgen05 family needs BLOCK_M 64, 128 or 256";
     return GPO_BAD_CONFIG;
   }
   if (BN != 32 && BN != 64 && BN != 128 && BN != 256) {
@@ -813,11 +812,9 @@ static gpo_status run_tc_dt(const gpo_key& k, const Plan& p, const gpo_args& a,
                             const LaunchCtx& c, CUtensorMapDataType dt) {
   if (p.aux[3]) return run_tc2_bn<T, FMT>(k, p, a, c, dt);
   const bool P = p.aux[2] != 0;
-  if constexpr (FMT != 2) {
-    if (k.block_m == 64)
-      return P ? run_tc_bn<T, FMT, 64, true>(k, p, a, c, dt)
-               : run_tc_bn<T, FMT, 64, false>(k, p, a, c, dt);
-  }
+  if (k.block_m == 64)
+    return P ? run_tc_bn<T, FMT, 64, true>(k, p, a, c, dt)
+             : run_tc_bn<T, FMT, 64, false>(k, p, a, c, dt);
   if (k.block_m == 128)
     return P ? run_tc_bn<T, FMT, 128, true>(k, p, a, c, dt)
              : run_tc_bn<T, FMT, 128, false>(k, p, a, c, dt);

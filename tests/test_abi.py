@@ -60,9 +60,8 @@ def test_block_m_64_uses_m64_tensor_core_mmas_for_16_bit_inputs():
     resp = mm({"BLOCK_M": 64, "BLOCK_N": 256}).resources()
     assert resp["kernel"] == "matmul_tc_kernel<bf16,64,256,persistent>"
     assert resp["tmem_cols"] == 512
-    # tf32 keeps M >= 128 MMAs: BLOCK_M 64 runs on the CUDA cores
     rt = mm({"BLOCK_M": 64, "BLOCK_N": 64, "num_warps": 4, "dtype": "tf32"}).resources()
-    assert rt["kernel"].startswith("matmul_simt")
+    assert rt["kernel"] == "matmul_tc_kernel<tf32,64,64,tile>"
 
 
 def test_shared_memory_overflow_is_a_compile_error():

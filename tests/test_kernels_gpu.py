@@ -54,7 +54,7 @@ MM_TC = [  # tcgen05 family: (BM, BN, BK, GROUP_M, warps, stages)
     (256, 256, 64, 8, 4, 3), (256, 128, 64, 4, 4, 3), (256, 32, 32, 1, 4, 2),
     (256, 256, 128, 8, 4, 2), (256, 256, 64, 8, 8, 6), (256, 128, 64, 16, 8, 8),
     (256, 64, 64, 1, 8, 4),
-    # BLOCK_M 64: M=64 MMAs (16-bit inputs; tf32 runs these on CUDA cores)
+    # BLOCK_M 64: M=64 MMAs
     (64, 128, 64, 8, 4, 4), (64, 256, 64, 8, 8, 4), (64, 64, 32, 1, 4, 3),
     (64, 32, 128, 4, 8, 2),
 ]
@@ -170,8 +170,7 @@ def test_tcgen05_matmul_ragged_shapes(shape, dtype):
         except KernelBuildError as e:
             assert "GPO_COMPILE_ERROR" in str(e), f"{cfg}: {e}"
             continue
-        want = "matmul_simt" if (t[0] == 64 and dtype == "tf32") else "matmul_tc"
-        assert kc.launch["kernel"].startswith(want), kc.launch["kernel"]
+        assert kc.launch["kernel"].startswith("matmul_tc"), kc.launch["kernel"]
         emu = O.emulate("matmul", shape, cfg, inputs)
         assert_close("matmul", dtype, out, emu, f"{shape} {cfg}")
 
