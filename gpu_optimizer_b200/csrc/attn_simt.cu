@@ -2,7 +2,8 @@
 //
 // Serves candidates the tensor-core family does not: dtype float32 (IEEE
 // fp32; the reference keeps ALLOW_TF32 off for attention,
-// compiler/triton/runner.py:237) and tiles other than BLOCK_M = 128.
+// compiler/triton/runner.py:237) and tiles other than BLOCK_M 64 / 128 /
+// 256 (BLOCK_M 16 or 32, BLOCK_N 16, head dims below 32, 2 warps).
 // Algorithm per (query tile, batch*head), as attention_kernel
 // (compiler/triton/kernels.py:212-270): stream K/V tiles of BLOCK_N keys,
 // online softmax with fp32 running max / sum, P cast to V's dtype before the
