@@ -37,7 +37,9 @@
 // tiles are zero-filled by TMA, so ragged M, N and K need no special path;
 // the epilogue masks the stores.
 #include <algorithm>
+#include <map>
 #include <mutex>
+#include <tuple>
 
 #include "gpo_common.cuh"
 #include "gpo_internal.h"
@@ -726,6 +728,50 @@ gpo_status plan_matmul_tc(const gpo_key& k, Plan& p, std::string& log) {
   return GPO_OK;
 }
 
+// CTAs of `func` that one SM holds at once, from the hardware limits:
+// shared memory (with the per-block reservation), registers (allocated per
+// warp in 256-register units), threads and TMEM columns.  Persistent grids
+// of the tensor-core kernels are sized with this: the runtime's occupancy
+// queries report one CTA per SM for these kernels although more are
+// resident at launch.  Cached per (device, kernel, block size, shared
+// memory, TMEM columns).
+static int resident_ctas_per_sm(const void* func, int threads, uint32_t dyn, uint32_t tmem_cols,
+                                int device) {
+  static std::mutex mu;
+  static std::map<std::tuple<int, const void*, int, uint32_t, uint32_t>, int> cache;
+  const auto key = std::make_tuple(device, func, threads, dyn, tmem_cols);
+  {
+    std::lock_guard<std::mutex> lk(mu);
+    auto it = cache.find(key);
+    if (it != cache.end()) return it->second;
+  }
+  cudaFuncAttributes fa;
+  int smem_sm = 0, reserved = 0, regs_sm = 0, thr_sm = 0;
+  if (cudaFuncGetAttributes(&fa, func) != cudaSuccess ||
+      cudaDeviceGetAttribute(&smem_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, device) !=
+          cudaSuccess ||
+      cudaDeviceGetAttribute(&reserved, cudaDevAttrReservedSharedMemoryPerBlock, device) !=
+          cudaSuccess ||
+      cudaDeviceGetAttribute(&regs_sm, cudaDevAttrMaxRegistersPerMultiprocessor, device) !=
+          cudaSuccess ||
+      cudaDeviceGetAttribute(&thr_sm, cudaDevAttrMaxThreadsPerMultiProcessor, device) !=
+          cudaSuccess) {
+    cudaGetLastError();
+    return 1;
+  }
+  const int64_t smem_cta = static_cast<int64_t>(dyn) + fa.sharedSizeBytes + reserved;
+  const int warps = (threads + 31) / 32;
+  const int64_t regs_warp = ((static_cast<int64_t>(fa.numRegs) * 32 + 255) / 256) * 256;
+  int64_t n = std::min<int64_t>(smem_sm / std::max<int64_t>(1, smem_cta),
+                                thr_sm / std::max(1, threads));
+  n = std::min<int64_t>(n, regs_sm / std::max<int64_t>(1, regs_warp * warps));
+  n = std::min<int64_t>(n, static_cast<int64_t>(kTmemCols) / std::max<uint32_t>(1u, tmem_cols));
+  const int r = static_cast<int>(std::max<int64_t>(1, n));
+  std::lock_guard<std::mutex> lk(mu);
+  cache[key] = r;
+  return r;
+}
+
 template <typename T, int FMT, int BM, int BN, bool P>
 static gpo_status run_tc(const gpo_key& k, const Plan& p, const gpo_args& a, const LaunchCtx& c,
                          CUtensorMapDataType dt) {
@@ -742,8 +788,14 @@ static gpo_status run_tc(const gpo_key& k, const Plan& p, const gpo_args& a, con
   gpo_status s = ensure_smem_attr(reinterpret_cast<const void*>(kern), dyn);
   if (s != GPO_OK) return s;
   const uint64_t tiles = cdiv(M, BM) * cdiv(N, BN);
+  // persistent: every CTA the SMs hold at once (TMEM, shared memory,
+  // registers), at most one per tile
   const unsigned grid =
-      P ? static_cast<unsigned>(std::min<uint64_t>(tiles, c.sm_count)) : static_cast<unsigned>(tiles);
+      P ? static_cast<unsigned>(std::min<uint64_t>(
+              tiles, static_cast<uint64_t>(c.sm_count) *
+                         resident_ctas_per_sm(reinterpret_cast<const void*>(kern), 256, dyn,
+                                              p.res.tmem_cols, c.device)))
+        : static_cast<unsigned>(tiles);
   kern<<<grid, P ? 256 : 128, dyn, c.stream>>>(ma, mb, static_cast<T*>(a.out),
                                                static_cast<int>(M), static_cast<int>(N),
                                                static_cast<int>(K), k.block_k, k.num_stages,
