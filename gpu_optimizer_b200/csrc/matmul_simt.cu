@@ -290,30 +290,39 @@ __global__ void __launch_bounds__(256) matmul_simt_async_kernel(const float* __r
       cp_async_commit();
     const float* As = sm + (ch % S) * stage;
     const float* Bs = As + BM * LDK;
-#pragma unroll 4
-    for (int kk = 0; kk < KC; ++kk) {
-      float a[TM], b[TN];
+    // A rows hold K contiguously (LDK = KC + 4 floats, 16-byte aligned):
+    // one 16-byte load gives a thread four K steps of one of its rows
+#pragma unroll 2
+    for (int k4 = 0; k4 < KC; k4 += 4) {
+      float4 a4[TM];
 #pragma unroll
-      for (int i = 0; i < TM; ++i) a[i] = As[(ty * TM + i) * LDK + kk];
-      if constexpr (TN % 4 == 0) {
+      for (int i = 0; i < TM; ++i)
+        a4[i] = *reinterpret_cast<const float4*>(As + (ty * TM + i) * LDK + k4);
 #pragma unroll
-        for (int j = 0; j < TN; j += 4) {
-          const float4 v = *reinterpret_cast<const float4*>(Bs + kk * BN + col_of(j));
-          b[j] = v.x; b[j + 1] = v.y; b[j + 2] = v.z; b[j + 3] = v.w;
-        }
-      } else {
+      for (int u = 0; u < 4; ++u) {
+        const int kk = k4 + u;
+        float b[TN];
+        if constexpr (TN % 4 == 0) {
 #pragma unroll
-        for (int j = 0; j < TN; ++j) b[j] = Bs[kk * BN + col_of(j)];
-      }
-#pragma unroll
-      for (int i = 0; i < TM; ++i) {
-        if constexpr (TN >= 2) {
-          const float2 ai = make_float2(a[i], a[i]);
-#pragma unroll
-          for (int j = 0; j < TP; ++j)
-            acc[i][j] = __ffma2_rn(ai, make_float2(b[2 * j], b[2 * j + 1]), acc[i][j]);
+          for (int j = 0; j < TN; j += 4) {
+            const float4 v = *reinterpret_cast<const float4*>(Bs + kk * BN + col_of(j));
+            b[j] = v.x; b[j + 1] = v.y; b[j + 2] = v.z; b[j + 3] = v.w;
+          }
         } else {
-          acc[i][0].x = fmaf(a[i], b[0], acc[i][0].x);
+#pragma unroll
+          for (int j = 0; j < TN; ++j) b[j] = Bs[kk * BN + col_of(j)];
+        }
+#pragma unroll
+        for (int i = 0; i < TM; ++i) {
+          const float ai = u == 0 ? a4[i].x : u == 1 ? a4[i].y : u == 2 ? a4[i].z : a4[i].w;
+          if constexpr (TN >= 2) {
+            const float2 ai2 = make_float2(ai, ai);
+#pragma unroll
+            for (int j = 0; j < TP; ++j)
+              acc[i][j] = __ffma2_rn(ai2, make_float2(b[2 * j], b[2 * j + 1]), acc[i][j]);
+          } else {
+            acc[i][0].x = fmaf(ai, b[0], acc[i][0].x);
+          }
         }
       }
     }
