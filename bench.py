@@ -485,6 +485,11 @@ def main():
         line = run_reference(args, rank, world)
         if rank == 0 and line is not None:
             print(json.dumps(line), flush=True)
+        if world > 1:
+            import torch.distributed as dist
+
+            # no barrier: the other ranks leave at once while rank 0 works
+            dist.destroy_process_group()
         return
     line = run_ours(args, rank, world, local)
     if not args.no_extras:
