@@ -149,30 +149,6 @@ unsigned persistent_grid(const void* func, int threads, size_t dyn_smem, int sm_
   return static_cast<unsigned>(std::max<int64_t>(1, std::min<int64_t>(g, work_items)));
 }
 
-unsigned persistent_clusters(const void* func, int threads, size_t dyn_smem, int64_t work_items) {
-  static std::mutex mu;
-  static std::map<std::tuple<const void*, int, size_t>, int> occ;
-  int clusters = 0;
-  {
-    std::lock_guard<std::mutex> lk(mu);
-    auto it = occ.find({func, threads, dyn_smem});
-    if (it != occ.end()) clusters = it->second;
-  }
-  if (clusters == 0) {
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(2, 1, 1);
-    cfg.blockDim = dim3(static_cast<unsigned>(threads), 1, 1);
-    cfg.dynamicSmemBytes = dyn_smem;
-    if (cudaOccupancyMaxActiveClusters(&clusters, func, &cfg) != cudaSuccess || clusters < 1) {
-      cudaGetLastError();
-      clusters = 1;
-    }
-    std::lock_guard<std::mutex> lk(mu);
-    occ[{func, threads, dyn_smem}] = clusters;
-  }
-  return static_cast<unsigned>(std::max<int64_t>(1, std::min<int64_t>(clusters, work_items)));
-}
-
 void* tensor_map_encoder() {
   static void* fn = nullptr;
   static std::once_flag once;

@@ -86,9 +86,6 @@ gpo_status ensure_smem_attr(const void* func, uint32_t dyn_smem);
 // of `func` at `threads` / `dyn_smem`, cached), at most `work_items`.
 unsigned persistent_grid(const void* func, int threads, size_t dyn_smem, int sm_count,
                          int64_t work_items);
-// Clusters of a __cluster_dims__ kernel that can be co-resident on the
-// device, capped at work_items (cached per kernel).
-unsigned persistent_clusters(const void* func, int threads, size_t dyn_smem, int64_t work_items);
 
 // Driver entry point for cuTensorMapEncodeTiled, resolved once.
 void* tensor_map_encoder();

@@ -821,8 +821,16 @@ static gpo_status run_tc2(const gpo_key& k, const Plan& p, const gpo_args& a, co
   if (s != GPO_OK) return s;
   const int64_t tiles = cdiv(M, 256) * cdiv(N, BN);
   const int threads = P ? 256 : 128;
+  // persistent: as many clusters as the SM pairs hold at once (TMEM, shared
+  // memory, registers; the cluster-occupancy query reports one CTA per SM
+  // for these kernels), at most one per tile
   const unsigned grid =
-      2u * (P ? persistent_clusters(reinterpret_cast<const void*>(kern), threads, dyn, tiles)
+      2u * (P ? static_cast<unsigned>(std::max<int64_t>(
+                    1, std::min<int64_t>(tiles, static_cast<int64_t>(c.sm_count / 2) *
+                                                    resident_ctas_per_sm(
+                                                        reinterpret_cast<const void*>(kern),
+                                                        threads, dyn, p.res.tmem_cols,
+                                                        c.device))))
               : static_cast<unsigned>(tiles));
   kern<<<grid, threads, dyn, c.stream>>>(ma, mb, static_cast<T*>(a.out), static_cast<int>(M),
                                      static_cast<int>(N), static_cast<int>(K), k.block_k,
