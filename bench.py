@@ -4,8 +4,10 @@
 Headline workload: C = A @ B, M = N = K = 4096, bf16 inputs ~ N(0,1)/sqrt(K),
 fp32 accumulation, bf16 output — the matmul configuration of the B200
 benchmark set, on the best configuration the search space offers for this
-backend (tcgen05, BLOCK_M 128, BLOCK_N 256, BLOCK_K 64, GROUP_M 8, 4 warps,
-2 stages: one output tile per CTA, two CTAs resident per SM).  One step = one matmul launch.
+backend (tcgen05, BLOCK_M 256, BLOCK_N 256, BLOCK_K 128, GROUP_M 16, 8 warps,
+3 stages: a persistent CTA pair per SM pair, M=256 cta_group::2 MMAs, two
+TMEM accumulators so each tile's epilogue overlaps the next tile's MMAs).
+One step = one matmul launch.
 Steps cycle over 4 independent input sets (4 x 96 MiB > 126 MB L2), so every
 launch streams its operands from HBM.
 
@@ -36,17 +38,18 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 SHAPE = (4096, 4096, 4096)
-BEST = {"BLOCK_M": 256, "BLOCK_N": 256, "BLOCK_K": 64, "GROUP_M": 16, "num_warps": 4,
+# persistent CTA pair (8 warps), 256 x 256 tiles, 128-deep K stages
+BEST = {"BLOCK_M": 256, "BLOCK_N": 256, "BLOCK_K": 128, "GROUP_M": 16, "num_warps": 8,
         "num_stages": 3, "dtype": "bfloat16"}
 FLOPS = 2.0 * SHAPE[0] * SHAPE[1] * SHAPE[2]
 N_SETS = 4
 METRIC = "matmul_bf16_4096_tflops"
 # DRAM bytes (read + write) per launch of the headline kernel from one ncu
 # capture of this exact kernel and configuration
-# (profiles/matmul_tc2_cta_pair_bf16_4096.md: 75.19 MB read + 11.55 MB
-# written); reported only while the headline runs that kernel.
-TRAFFIC_KERNEL = "matmul_tc2_kernel<bf16,256,256,cta_pair>"
-TRAFFIC_BYTES_PER_LAUNCH = 86_740_000
+# (profiles/matmul_tc2_cta_pair_persistent_bf16_4096.md: 69.61 MB read +
+# 14.26 MB written); reported only while the headline runs that kernel.
+TRAFFIC_KERNEL = "matmul_tc2_kernel<bf16,256,256,cta_pair_persistent>"
+TRAFFIC_BYTES_PER_LAUNCH = 83_875_000
 
 
 def parse_args():

@@ -14,6 +14,9 @@ pytestmark = pytest.mark.gpu
 MM_FULL = [
     {"BLOCK_M": 256, "BLOCK_N": 256, "BLOCK_K": 64, "GROUP_M": 16, "num_warps": 4,
      "num_stages": 3, "dtype": "bfloat16"},
+    # the bench headline: persistent pair, 128-deep K stages
+    {"BLOCK_M": 256, "BLOCK_N": 256, "BLOCK_K": 128, "GROUP_M": 16, "num_warps": 8,
+     "num_stages": 3, "dtype": "bfloat16"},
     {"BLOCK_M": 256, "BLOCK_N": 256, "BLOCK_K": 64, "GROUP_M": 16, "num_warps": 8,
      "num_stages": 6, "dtype": "bfloat16"},
     {"BLOCK_M": 128, "BLOCK_N": 256, "BLOCK_K": 64, "GROUP_M": 8, "num_warps": 8,
@@ -21,7 +24,7 @@ MM_FULL = [
 ]
 
 
-@pytest.mark.parametrize("MM_BEST", MM_FULL, ids=lambda c: f"{c['BLOCK_M']}x{c['BLOCK_N']}w{c['num_warps']}")
+@pytest.mark.parametrize("MM_BEST", MM_FULL, ids=lambda c: f"{c['BLOCK_M']}x{c['BLOCK_N']}x{c['BLOCK_K']}w{c['num_warps']}s{c['num_stages']}")
 def test_matmul_4096_linearity_and_reference(MM_BEST):
     task = get_task("matmul", "b200")
     shape = (4096, 4096, 4096)
