@@ -427,8 +427,8 @@ EXTRA_TASKS = [
                                             "num_stages": 2, "dtype": "bfloat16"}),
     ("attention", (128, 4096, 128), {"BLOCK_M": 128, "BLOCK_N": 128, "num_warps": 4,
                                      "num_stages": 2, "dtype": "bfloat16"}),
-    ("matmul", (8192, 8192, 8192), {"BLOCK_M": 256, "BLOCK_N": 256, "BLOCK_K": 64,
-                                    "GROUP_M": 16, "num_warps": 4, "num_stages": 3,
+    ("matmul", (8192, 8192, 8192), {"BLOCK_M": 256, "BLOCK_N": 256, "BLOCK_K": 128,
+                                    "GROUP_M": 16, "num_warps": 8, "num_stages": 3,
                                     "dtype": "bfloat16"}),
 ]
 
