@@ -45,9 +45,8 @@ FLOPS = 2.0 * SHAPE[0] * SHAPE[1] * SHAPE[2]
 N_SETS = 4
 METRIC = "matmul_bf16_4096_tflops"
 # DRAM bytes (read + write) per launch of the headline kernel from one ncu
-# capture of this exact kernel and configuration
-# (profiles/matmul_tc2_cta_pair_persistent_bf16_4096.md: 69.61 MB read +
-# 14.26 MB written); reported only while the headline runs that kernel.
+# capture of this exact kernel and configuration (69.61 MB read + 14.26 MB
+# written); reported only while the headline runs that kernel.
 TRAFFIC_KERNEL = "matmul_tc2_kernel<bf16,256,256,cta_pair_persistent>"
 TRAFFIC_BYTES_PER_LAUNCH = 83_875_000
 
