@@ -530,6 +530,414 @@ __global__ void __launch_bounds__(128 + 128 * WG,
   }
 }
 
+// ------------------------------------------------ two query tiles per CTA
+// BLOCK_M 256 with num_warps 8: one CTA per (256-row query span, head)
+// works on two 128-row query tiles, t = 0 and 1, that share every K/V
+// block.  TMEM holds O_t in columns [t*D, t*D + D) and one S/P buffer per
+// tile in [2D + t*BN, 2D + (t+1)*BN).  The MMA thread alternates the tiles
+//     ... PV_0(j), S_0(j+1), PV_1(j), S_1(j+1), PV_0(j+1), S_0(j+2) ...
+// so while softmax warpgroup t turns S_t(j) into P_t(j), the tensor pipe
+// runs the other tile's PV and S MMAs: each tile's chain S -> softmax -> PV
+// overlaps the other's, and every SM sub-partition holds one softmax warp
+// of each tile.  S_t(j+1) is written over P_t(j) only after PV_t(j) was
+// issued (tcgen05 MMAs of one thread execute in issue order).
+// Warps: 0 TMA of Q (both tiles, once) and the K ring, 3 TMA of the V ring,
+// 1 MMA issuer, 2 TMEM owner, 4-7 softmax of tile 0 (TMEM lanes = rows),
+// 8-11 softmax of tile 1.  The softmax is the one-tile kernel's: running
+// max in the log2 domain moved (with the O rescale) only past the lazy
+// threshold, P = exp2(s - m) as 16-bit pairs into TMEM, fp32 row sums;
+// each softmax warpgroup writes its tile's output.
+struct AttnDualShared {
+  uint64_t q_full;
+  uint64_t k_full[kAttnMaxStages];
+  uint64_t k_empty[kAttnMaxStages];
+  uint64_t v_full[kAttnMaxStages];
+  uint64_t v_empty[kAttnMaxStages];
+  uint64_t s_full[2];
+  uint64_t p_full[2];
+  uint64_t pv_done[2];
+  uint64_t drain;
+  uint32_t tmem_base;
+  int abort;
+};
+
+constexpr int kAttnDualThreads = 384;
+// Register split: the kernel launches at 65536 / 384 = 168 registers per
+// thread (64512 for the CTA); the warpgroup of producers, MMA issuer and
+// TMEM owner gives back down to kAttnDualLowRegs and each softmax
+// warpgroup (a 128-column S row per thread) grows to kAttnDualHighRegs:
+// 128 * 56 + 256 * 224 = 64512, the launch's total, so every increase
+// is covered.
+constexpr int kAttnDualLowRegs = 56;
+constexpr int kAttnDualHighRegs = 224;
+static_assert(128 * kAttnDualLowRegs + 256 * kAttnDualHighRegs <= 168 * kAttnDualThreads,
+              "register split exceeds the launch's registers");
+
+template <int N>
+__device__ __forceinline__ void regs_dec() {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
+}
+template <int N>
+__device__ __forceinline__ void regs_inc() {
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
+}
+
+template <int D>
+struct AttnDualGeom {
+  static constexpr int ES = 2;
+  static constexpr int SW = (D * ES) < 128 ? (D * ES) : 128;  // swizzle of Q/K/V rows
+  static constexpr uint32_t Q_BYTES = 128u * D * ES;           // one query tile
+};
+
+// TMA producer of Q (both tiles) and the K ring (is_k), or of the V ring.
+template <int BN, int D>
+__device__ __forceinline__ void attn_dual_producer(const CUtensorMap* tma_q,
+                                                   const CUtensorMap* map, AttnDualShared& sh,
+                                                   uint32_t q_smem, uint32_t ring, int q0, int bh,
+                                                   int nblk, int stages, bool is_k,
+                                                   volatile int* abort_flag, unsigned int* err) {
+  using G = AttnDualGeom<D>;
+  constexpr uint32_t KV_BYTES = static_cast<uint32_t>(BN) * D * G::ES;
+  constexpr uint32_t KV_SLOT = (KV_BYTES + 1023u) & ~1023u;
+  uint64_t* full = is_k ? sh.k_full : sh.v_full;
+  uint64_t* empty = is_k ? sh.k_empty : sh.v_empty;
+  bool ok = true;
+  int issued = 0;
+  if (is_k) {
+    mbar_arrive_expect_tx(smem_u32(&sh.q_full), 2u * G::Q_BYTES);
+#pragma unroll
+    for (int t = 0; t < 2; ++t)
+#pragma unroll
+      for (int a = 0; a < (D * G::ES) / G::SW; ++a)
+        tma_load_3d(q_smem + t * G::Q_BYTES + a * 128 * G::SW, tma_q, smem_u32(&sh.q_full),
+                    a * (G::SW / G::ES), q0 + 128 * t, bh);
+  }
+  for (int j = 0; j < nblk; ++j) {
+    const int s = j % stages;
+    const uint32_t r = static_cast<uint32_t>(j / stages);
+    if (!mbar_wait(smem_u32(&empty[s]), (r & 1u) ^ 1u, abort_flag, err, kErrWaitProducer)) {
+      ok = false;
+      break;
+    }
+    const uint32_t dst = ring + static_cast<uint32_t>(s) * KV_SLOT;
+    mbar_arrive_expect_tx(smem_u32(&full[s]), KV_BYTES);
+    // K: rows [j*BN, +BN) in K-major atoms; V: the same rows, MN-major
+    // column chunks (the B operand of the PV MMA)
+#pragma unroll
+    for (int a = 0; a < (D * G::ES) / G::SW; ++a)
+      tma_load_3d(dst + a * BN * G::SW, map, smem_u32(&full[s]), a * (G::SW / G::ES), j * BN, bh);
+    issued = j + 1;
+  }
+  if (!ok) {
+    if (is_k) mbar_wait_drain(smem_u32(&sh.q_full), 0, err);
+    for (int j = max(0, issued - stages); j < issued; ++j)
+      mbar_wait_drain(smem_u32(&full[j % stages]), static_cast<uint32_t>(j / stages) & 1u, err);
+  }
+}
+
+// MMA issuer: S_t(j) = Q_t K_j^T and O_t += P_t(j) V_j, tiles alternating.
+template <int FMT, int BN, int D>
+__device__ __forceinline__ void attn_dual_mma(AttnDualShared& sh, uint32_t tmem, uint32_t q_smem,
+                                              uint32_t k_smem, uint32_t v_smem, int nb0, int nb1,
+                                              int stages, volatile int* abort_flag,
+                                              unsigned int* err) {
+  using G = AttnDualGeom<D>;
+  constexpr int SW = G::SW;
+  constexpr uint32_t KV_SLOT = ((static_cast<uint32_t>(BN) * D * G::ES) + 1023u) & ~1023u;
+  constexpr uint32_t IDESC_S = make_idesc(FMT, 128, BN, false, false);
+  constexpr uint32_t IDESC_O = make_idesc(FMT, 128, D, false, true);
+  bool ok = mbar_wait(smem_u32(&sh.q_full), 0, abort_flag, err, kErrWaitMma);
+  auto s_mma = [&](int t, int j) {
+    const uint32_t ks = k_smem + static_cast<uint32_t>(j % stages) * KV_SLOT;
+    const uint32_t qs = q_smem + static_cast<uint32_t>(t) * G::Q_BYTES;
+    const uint32_t s_tmem = tmem + static_cast<uint32_t>(2 * D + t * BN);
+#pragma unroll
+    for (int kk = 0; kk < D / 16; ++kk) {
+      const uint32_t kbyte = static_cast<uint32_t>(kk) * 32u;
+      const uint32_t aoff = (kbyte / SW) * (128 * SW) + (kbyte % SW);
+      const uint32_t boff = (kbyte / SW) * (BN * SW) + (kbyte % SW);
+      mma_f16_ss(s_tmem, make_smem_desc(qs + aoff, 16, 8 * SW, SW),
+                 make_smem_desc(ks + boff, 16, 8 * SW, SW), IDESC_S, kk > 0 ? 1u : 0u);
+    }
+    mma_commit(smem_u32(&sh.s_full[t]));
+  };
+  // P_t sits in the first BN/2 columns of tile t's S/P buffer
+  auto pv_mma = [&](int t, int j) {
+    const uint32_t vs = v_smem + static_cast<uint32_t>(j % stages) * KV_SLOT;
+    const uint32_t pa = tmem + static_cast<uint32_t>(2 * D + t * BN);
+    const uint32_t o_tmem = tmem + static_cast<uint32_t>(t * D);
+#pragma unroll
+    for (int kk = 0; kk < BN / 16; ++kk) {
+      const uint64_t bdesc = make_smem_desc(vs + kk * 16 * SW, BN * SW, 8 * SW, SW);
+      mma_f16_ts(o_tmem, pa + static_cast<uint32_t>(kk * 8), bdesc, IDESC_O,
+                 (j > 0 || kk > 0) ? 1u : 0u);
+    }
+    mma_commit(smem_u32(&sh.pv_done[t]));
+  };
+  if (ok) ok = mbar_wait(smem_u32(&sh.k_full[0]), 0, abort_flag, err, kErrWaitMma);
+  if (ok) {
+    tc_fence_after();
+    s_mma(0, 0);
+    s_mma(1, 0);
+    mma_commit(smem_u32(&sh.k_empty[0]));
+  }
+  for (int j = 0; j < nb1 && ok; ++j) {
+    const int sv = j % stages;
+    if (!mbar_wait(smem_u32(&sh.v_full[sv]), static_cast<uint32_t>(j / stages) & 1u, abort_flag,
+                   err, kErrWaitMma)) {
+      ok = false;
+      break;
+    }
+    bool k_ready = false;
+#pragma unroll
+    for (int t = 0; t < 2; ++t) {
+      const int nbt = t == 0 ? nb0 : nb1;
+      if (ok && j < nbt) {
+        ok = mbar_wait(smem_u32(&sh.p_full[t]), static_cast<uint32_t>(j) & 1u, abort_flag, err,
+                       kErrWaitMma);
+        if (ok) {
+          tc_fence_after();
+          pv_mma(t, j);
+        }
+      }
+      if (ok && j + 1 < nbt) {
+        if (!k_ready) {
+          const int sk = (j + 1) % stages;
+          ok = mbar_wait(smem_u32(&sh.k_full[sk]), static_cast<uint32_t>((j + 1) / stages) & 1u,
+                         abort_flag, err, kErrWaitMma);
+          tc_fence_after();
+          k_ready = true;
+        }
+        if (ok) s_mma(t, j + 1);
+      }
+    }
+    if (!ok) break;
+    mma_commit(smem_u32(&sh.v_empty[sv]));
+    if (j + 1 < nb1) mma_commit(smem_u32(&sh.k_empty[(j + 1) % stages]));
+  }
+  if (!ok) {
+    mma_commit(smem_u32(&sh.drain));
+    mbar_wait_drain(smem_u32(&sh.drain), 0, err);
+  }
+}
+
+// Softmax and epilogue of tile t = (warp - 4) / 4; thread = query row =
+// TMEM lane.
+template <typename T, int FMT, int BN, int D, bool CAUSAL>
+__device__ __forceinline__ void attn_dual_softmax(AttnDualShared& sh, uint32_t tmem,
+                                                  T* __restrict__ O, int S, int q0, int bh,
+                                                  int nb0, int nb1, float scale_log2, int warp,
+                                                  int lane, volatile int* abort_flag,
+                                                  unsigned int* err) {
+  const int t = (warp - 4) >> 2;
+  const int q = warp & 3;  // TMEM lane quarter
+  const int row = q * 32 + lane;
+  const int tile_first = q0 + 128 * t;
+  const int qrow = tile_first + row;
+  const int nblk = t == 0 ? nb0 : nb1;
+  const uint32_t lane_addr = static_cast<uint32_t>(q * 32) << 16;
+  const uint32_t sp = tmem + lane_addr + static_cast<uint32_t>(2 * D + t * BN);
+  const uint32_t o_tmem = tmem + lane_addr + static_cast<uint32_t>(t * D);
+  const float2 scale2 = make_float2(scale_log2, scale_log2);
+  float m_used = -INFINITY;
+  float l = 0.f;
+  bool ok = true;
+  for (int j = 0; j < nblk; ++j) {
+    if (!mbar_wait(smem_u32(&sh.s_full[t]), static_cast<uint32_t>(j) & 1u, abort_flag, err,
+                   kErrWaitSoftmax))
+      ok = false;
+    if (!__all_sync(0xffffffffu, ok)) {
+      ok = false;
+      break;
+    }
+    tc_fence_after();
+    uint32_t sv[BN];
+#pragma unroll
+    for (int c = 0; c < BN / 32; ++c)
+      tmem_ld32(sp + static_cast<uint32_t>(c * 32), *reinterpret_cast<uint32_t(*)[32]>(sv + c * 32));
+    tmem_wait_ld();
+    auto f = [&](int i) { return __uint_as_float(sv[i]); };
+    const int key0 = j * BN;
+    if (key0 + BN > S || (CAUSAL && key0 + BN - 1 > tile_first)) {
+#pragma unroll
+      for (int i = 0; i < BN; ++i) {
+        const int key = key0 + i;
+        if (key >= S || (CAUSAL && key > qrow)) sv[i] = __float_as_uint(-INFINITY);
+      }
+    }
+    float mx[4] = {f(0), f(1), f(2), f(3)};
+#pragma unroll
+    for (int i = 4; i + 1 < BN; i += 2) mx[(i >> 1) & 3] = fmax3(mx[(i >> 1) & 3], f(i), f(i + 1));
+    const float mb = fmaxf(fmax3(mx[0], mx[1], mx[2]), mx[3]) * scale_log2;
+    if (j == 0) {
+      m_used = mb;
+    } else {
+      const bool need = mb > m_used + kRescaleThreshold;
+      if (__any_sync(0xffffffffu, need)) {
+        const float m_new = need ? mb : m_used;
+        const float alpha = ex2_approx(m_used - m_new);
+        // O_t holds PV_t(0..j-1); wait for PV_t(j-1) before rescaling it
+        ok = mbar_wait(smem_u32(&sh.pv_done[t]), static_cast<uint32_t>(j - 1) & 1u, abort_flag,
+                       err, kErrWaitSoftmax);
+        if (!__all_sync(0xffffffffu, ok)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+#pragma unroll 1
+        for (int c = 0; c < D / 16; ++c) {
+          uint32_t r[16];
+          const uint32_t addr = o_tmem + static_cast<uint32_t>(c * 16);
+          tmem_ld16(addr, r);
+          tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 16; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha);
+          tmem_st16(addr, r);
+        }
+        tmem_wait_st();
+        l *= alpha;
+        m_used = m_new;
+      }
+    }
+    const float neg_m = (m_used == -INFINITY) ? 0.f : -m_used;
+    const float2 shift2 = make_float2(neg_m, neg_m);
+    float2 rs[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f),
+                    make_float2(0.f, 0.f)};
+    // P_t(j) over the first BN/2 columns of the buffer, 16 columns as soon
+    // as they are packed
+#pragma unroll
+    for (int c = 0; c < BN / 32; ++c) {
+      uint32_t pk[16];
+#pragma unroll
+      for (int g2 = 0; g2 < 16; ++g2) {
+        const int g = c * 16 + g2;
+        const float2 x = __ffma2_rn(make_float2(f(2 * g), f(2 * g + 1)), scale2, shift2);
+        const float2 p = make_float2(ex2_approx(x.x), ex2_approx(x.y));  // -inf -> 0
+        rs[g & 3] = __fadd2_rn(rs[g & 3], p);
+        pk[g2] = FMT == 1 ? pack_bf16(p.x, p.y) : pack_f16(p.x, p.y);
+      }
+      tmem_st16(sp + static_cast<uint32_t>(c * 16), pk);
+    }
+    const float2 rsum = __fadd2_rn(__fadd2_rn(rs[0], rs[1]), __fadd2_rn(rs[2], rs[3]));
+    l += rsum.x + rsum.y;
+    tmem_wait_st();
+    tc_fence_before();
+    __syncwarp();
+    if (lane == 0) mbar_arrive(smem_u32(&sh.p_full[t]));
+  }
+  // ------------------------------------------------------------ epilogue
+  if (ok && nblk > 0)
+    ok = mbar_wait(smem_u32(&sh.pv_done[t]), static_cast<uint32_t>(nblk - 1) & 1u, abort_flag,
+                   err, kErrWaitSoftmax);
+  if (__all_sync(0xffffffffu, ok)) {
+    tc_fence_after();
+    const float inv_l = l > 0.f ? 1.0f / l : 0.f;
+    T* orow = O + (static_cast<int64_t>(bh) * S + qrow) * D;
+#pragma unroll 1
+    for (int c = 0; c < D / 16; ++c) {
+      uint32_t r[16];
+      tmem_ld16(o_tmem + static_cast<uint32_t>(c * 16), r);
+      tmem_wait_ld();
+      if (qrow < S) {
+        uint32_t pk[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const float lo = __uint_as_float(r[2 * i]) * inv_l;
+          const float hi = __uint_as_float(r[2 * i + 1]) * inv_l;
+          pk[i] = FMT == 1 ? pack_bf16(lo, hi) : pack_f16(lo, hi);
+        }
+        uint4* d4 = reinterpret_cast<uint4*>(orow + c * 16);
+        d4[0] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+        d4[1] = make_uint4(pk[4], pk[5], pk[6], pk[7]);
+      }
+    }
+  }
+}
+
+template <typename T, int FMT, int BN, int D, bool CAUSAL>
+__global__ void __launch_bounds__(kAttnDualThreads, 1)
+    attn_tc_dual_kernel(const __grid_constant__ CUtensorMap tma_q,
+                        const __grid_constant__ CUtensorMap tma_k,
+                        const __grid_constant__ CUtensorMap tma_v, T* __restrict__ O, int S,
+                        int stages, float scale_log2, unsigned int* err) {
+  using G = AttnDualGeom<D>;
+  constexpr uint32_t KV_SLOT = ((static_cast<uint32_t>(BN) * D * G::ES) + 1023u) & ~1023u;
+  constexpr int COLS = 2 * D + 2 * BN;
+  constexpr int ALLOC = attn_tmem_alloc(COLS);
+  static_assert(COLS <= 512, "TMEM holds 512 columns");
+  static_assert(BN % 32 == 0 && D % 32 == 0, "TMEM accesses of 32 columns");
+
+  __shared__ AttnDualShared sh;
+  extern __shared__ uint8_t dyn_smem[];
+  const uint32_t base = (smem_u32(dyn_smem) + 1023u) & ~1023u;
+  const uint32_t q_smem = base;  // tile t at q_smem + t * Q_BYTES
+  const uint32_t k_smem = q_smem + 2u * G::Q_BYTES;
+  const uint32_t v_smem = k_smem + static_cast<uint32_t>(stages) * KV_SLOT;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int spans = (S + 255) / 256;
+  // longest causal spans first; identity order for the non-causal task
+  const int span = CAUSAL ? (spans - 1 - static_cast<int>(blockIdx.x))
+                          : static_cast<int>(blockIdx.x);
+  const int q0 = span * 256;  // tile t: query rows [q0 + 128 t, +128)
+  const int bh = blockIdx.y;
+  auto blocks_of = [&](int t) {
+    const int len = CAUSAL ? min(S, q0 + 128 * (t + 1)) : S;
+    return (len + BN - 1) / BN;
+  };
+  const int nb0 = blocks_of(0), nb1 = blocks_of(1);  // nb0 <= nb1
+
+  if (threadIdx.x == 0) {
+    mbar_init(smem_u32(&sh.q_full), 1);
+    for (int s = 0; s < stages; ++s) {
+      mbar_init(smem_u32(&sh.k_full[s]), 1);
+      mbar_init(smem_u32(&sh.k_empty[s]), 1);
+      mbar_init(smem_u32(&sh.v_full[s]), 1);
+      mbar_init(smem_u32(&sh.v_empty[s]), 1);
+    }
+    for (int t = 0; t < 2; ++t) {
+      mbar_init(smem_u32(&sh.s_full[t]), 1);
+      mbar_init(smem_u32(&sh.p_full[t]), 4);
+      mbar_init(smem_u32(&sh.pv_done[t]), 1);
+    }
+    mbar_init(smem_u32(&sh.drain), 1);
+    sh.abort = 0;
+    fence_barrier_init();
+    tma_prefetch_desc(&tma_q);
+    tma_prefetch_desc(&tma_k);
+    tma_prefetch_desc(&tma_v);
+  }
+  if (warp == 2) {
+    tmem_alloc(smem_u32(&sh.tmem_base), ALLOC);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = sh.tmem_base;
+  volatile int* abort_flag = &sh.abort;
+  // Register split by whole warpgroups; each setmaxnreg heads its role's
+  // branch so that the register allocator gives that code the new budget.
+  if (warp < 4) {
+    regs_dec<kAttnDualLowRegs>();
+    if ((warp == 0 || warp == 3) && lane == 0)
+      attn_dual_producer<BN, D>(&tma_q, warp == 0 ? &tma_k : &tma_v, sh, q_smem,
+                                warp == 0 ? k_smem : v_smem, q0, bh, nb1, stages, warp == 0,
+                                abort_flag, err);
+    else if (warp == 1 && lane == 0)
+      attn_dual_mma<FMT, BN, D>(sh, tmem, q_smem, k_smem, v_smem, nb0, nb1, stages, abort_flag,
+                                err);
+  } else {
+    regs_inc<kAttnDualHighRegs>();
+    attn_dual_softmax<T, FMT, BN, D, CAUSAL>(sh, tmem, O, S, q0, bh, nb0, nb1, scale_log2, warp,
+                                             lane, abort_flag, err);
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 2) tmem_dealloc(tmem, ALLOC);
+}
+
 // ------------------------------------------------------------------- host
 typedef CUresult (*EncodeTiledFn3)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
                                    const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
@@ -570,7 +978,56 @@ static uint32_t attn_tc_smem(int BN, int D, int stages, bool pair, int tm) {
 // num_warps 4 -> one softmax warpgroup; 8 -> two splitting each row's
 // columns (BLOCK_N >= 64; with BLOCK_N 32 a warp would hold fewer than the
 // 32 columns of one TMEM access, so the kernel keeps one warpgroup).
+static uint32_t attn_dual_smem(int BN, int D, int stages) {
+  auto al = [](uint32_t x) { return (x + 1023u) & ~1023u; };
+  const uint32_t q = 2u * 128u * static_cast<uint32_t>(D) * 2u;
+  const uint32_t kv = static_cast<uint32_t>(BN) * D * 2u;
+  return al(q) + static_cast<uint32_t>(stages) * 2 * al(kv) + 1024u;
+}
+
+// BLOCK_M 256 with num_warps 8: two 128-row query tiles per CTA
+// (attn_tc_dual_kernel); aux[2] = 2 marks it.
+static gpo_status plan_attention_dual(const gpo_key& k, Plan& p, std::string& log) {
+  const int D = static_cast<int>(k.shape[2]);
+  const int BN = k.block_n;
+  if (k.num_stages < 1 || k.num_stages > kAttnMaxStages) {
+    log = "num_stages must be in [1, 4]";
+    return GPO_BAD_CONFIG;
+  }
+  const int cols = 2 * D + 2 * BN;
+  if (cols > static_cast<int>(kTmemCols)) {
+    log = "TMEM needs " + std::to_string(cols) + " columns (2 O tiles x " + std::to_string(D) +
+          " + 2 S buffers x " + std::to_string(BN) + ") > 512";
+    return GPO_COMPILE_ERROR;
+  }
+  const uint32_t dyn = attn_dual_smem(BN, D, k.num_stages);
+  const uint32_t smem = dyn + static_cast<uint32_t>(sizeof(AttnDualShared));
+  if (smem > kMaxSmemPerCta) {
+    log = "shared memory " + std::to_string(smem) + " B (2 Q tiles + " +
+          std::to_string(k.num_stages) + " K and V stages) exceeds the 232448 B per-CTA limit";
+    return GPO_COMPILE_ERROR;
+  }
+  p.aux[0] = static_cast<int>(dyn);
+  p.aux[1] = 1;
+  p.aux[2] = 2;
+  p.aux[3] = 1;
+  p.aux[4] = 128;
+  p.family = "attn_tc";
+  p.res.smem_bytes = smem;
+  p.res.tmem_cols = static_cast<uint32_t>(attn_tmem_alloc(cols));
+  p.res.threads_per_cta = static_cast<uint32_t>(kAttnDualThreads);
+  p.res.grid_x = static_cast<uint32_t>(cdiv(k.shape[1], 256));
+  p.res.grid_y = static_cast<uint32_t>(k.shape[0]);
+  p.res.grid_z = 1;
+  p.res.launches_per_call = 1;
+  snprintf(p.res.kernel, sizeof(p.res.kernel), "attn_tc_dual_kernel<%s,BN=%d,D=%d,%s,two_tiles>",
+           k.dtype == GPO_BFLOAT16 ? "bf16" : "f16", BN, D,
+           k.task == GPO_TASK_ATTENTION_CAUSAL ? "causal" : "full");
+  return GPO_OK;
+}
+
 gpo_status plan_attention_tc(const gpo_key& k, Plan& p, std::string& log) {
+  if (k.block_m == 256 && k.num_warps == 8) return plan_attention_dual(k, p, log);
   const int D = static_cast<int>(k.shape[2]);
   const int BN = k.block_n;
   const bool pair = k.block_m == 256;
@@ -665,8 +1122,34 @@ static gpo_status run_attn_tc_wg(const gpo_key& k, const Plan& p, const gpo_args
 }
 
 template <typename T, int FMT, int BN, int D, bool CAUSAL>
+static gpo_status run_attn_tc_dual(const gpo_key& k, const Plan& p, const gpo_args& a,
+                                   const LaunchCtx& c, CUtensorMapDataType dt) {
+  const uint64_t BH = static_cast<uint64_t>(k.shape[0]), S = static_cast<uint64_t>(k.shape[1]);
+  constexpr int SW = (D * 2) < 128 ? (D * 2) : 128;
+  CUtensorMap mq, mk, mv;
+  if (!encode_bsd(&mq, dt, a.in[0], BH, S, D, 128, SW) ||
+      !encode_bsd(&mk, dt, a.in[1], BH, S, D, BN, SW) ||
+      !encode_bsd(&mv, dt, a.in[2], BH, S, D, BN, SW))
+    return GPO_LAUNCH_ERROR;
+  auto kern = attn_tc_dual_kernel<T, FMT, BN, D, CAUSAL>;
+  const uint32_t dyn = static_cast<uint32_t>(p.aux[0]);
+  gpo_status s = ensure_smem_attr(reinterpret_cast<const void*>(kern), dyn);
+  if (s != GPO_OK) return s;
+  const dim3 grid(static_cast<unsigned>(cdiv(S, 256)), static_cast<unsigned>(BH));
+  const float scale_log2 = 1.4426950408889634f / sqrtf(static_cast<float>(D));
+  kern<<<grid, kAttnDualThreads, dyn, c.stream>>>(mq, mk, mv, static_cast<T*>(a.out),
+                                                  static_cast<int>(S), k.num_stages, scale_log2,
+                                                  c.err);
+  return launch_status();
+}
+
+template <typename T, int FMT, int BN, int D, bool CAUSAL>
 static gpo_status run_attn_tc(const gpo_key& k, const Plan& p, const gpo_args& a,
                               const LaunchCtx& c, CUtensorMapDataType dt) {
+  if (p.aux[2] == 2) {
+    if constexpr (2 * D + 2 * BN <= 512) return run_attn_tc_dual<T, FMT, BN, D, CAUSAL>(k, p, a, c, dt);
+    return GPO_INTERNAL;  // rejected by the plan (TMEM)
+  }
   if constexpr (D + 2 * BN <= 512) {
     constexpr int NB = attn_sbufs(D, BN);
     const bool pair = p.aux[2] != 0;
@@ -687,9 +1170,12 @@ static gpo_status run_attn_tc(const gpo_key& k, const Plan& p, const gpo_args& a
     }
     if (p.aux[3] != NB) return GPO_INTERNAL;
     if constexpr (BN >= 64) {
-      if (p.aux[1] == 2)
-        return pair ? run_attn_tc_wg<T, FMT, BN, D, CAUSAL, 2, true, NB>(k, p, a, c, dt)
-                    : run_attn_tc_wg<T, FMT, BN, D, CAUSAL, 2, false, NB>(k, p, a, c, dt);
+      // two softmax warpgroups: one 128-row tile per CTA (BLOCK_M 256 with
+      // 8 warps is the two-tile kernel)
+      if (p.aux[1] == 2) {
+        if (pair) return GPO_INTERNAL;
+        return run_attn_tc_wg<T, FMT, BN, D, CAUSAL, 2, false, NB>(k, p, a, c, dt);
+      }
     }
     if (p.aux[1] != 1) return GPO_INTERNAL;
     return pair ? run_attn_tc_wg<T, FMT, BN, D, CAUSAL, 1, true, NB>(k, p, a, c, dt)

@@ -449,11 +449,13 @@ gpo_status launch_selftest_timeout(const LaunchCtx& c, unsigned long long limit_
 
 // ------------------------------------------------- allocation-free two_pass
 // Some callers cannot allocate device memory at the point where they need a
-// sum: code running inside a CUDA stream capture that must not add
-// allocations to the graph, host runtimes with their own fixed device-memory
-// budget, or plug-in hosts that hand this library only input and output
-// buffers.  For them gpo_reduction_sum_noalloc runs the two_pass reduction
-// with its partial sums in the fixed array below instead of a caller buffer.
+// sum: plug-in hosts that own all device memory and hand this library only
+// input and output buffers (an allocation would escape the host's
+// accounting and can fail under its memory cap), and latency-critical
+// callers that cannot take the device synchronisation a cudaMalloc /
+// cudaFree pair can cause.  For them gpo_reduction_sum_noalloc runs the
+// two_pass reduction with its partial sums in the fixed array below instead
+// of a caller buffer.
 //
 // The array is part of the library image: every GPU that loads the library
 // holds it (256 KiB) until the process exits.  All calls on a device share
@@ -466,13 +468,42 @@ static __device__ __align__(256) float g_noalloc_partials[kNoAllocMaxPartials];
 
 namespace {
 constexpr int kNoAllocDevices = 64;
+// The array's address belongs to one context of the device: the cache
+// entry records that context and is looked up again when the device's
+// current context differs (a context recreated after cudaDeviceReset maps
+// the library image afresh).
+struct NoAllocSlot {
+  void* ctx;
+  float* ptr;
+};
 std::mutex g_noalloc_mu;
-float* g_noalloc_ptr[kNoAllocDevices] = {nullptr};
+NoAllocSlot g_noalloc[kNoAllocDevices] = {};
+
+using CtxGetCurrentFn = int (*)(void**);  // cuCtxGetCurrent(CUcontext*)
+
+// The calling thread's current context, or nullptr when none is current or
+// the driver entry point is unavailable (the address is then looked up on
+// every call).
+void* current_context() {
+  static CtxGetCurrentFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+    void* f = nullptr;
+    if (cudaGetDriverEntryPointByVersion("cuCtxGetCurrent", &f, 12000, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<CtxGetCurrentFn>(f);
+  });
+  void* ctx = nullptr;
+  if (fn == nullptr || fn(&ctx) != 0) return nullptr;
+  return ctx;
+}
 }  // namespace
 
 // Device address of g_noalloc_partials on the current device.  In host code
 // the array's name is only a host-side stand-in, so the address is resolved
-// once per device with that device current.
+// with the device current: once per device and context.
 static gpo_status noalloc_scratch(float** out) {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) {
@@ -481,16 +512,19 @@ static gpo_status noalloc_scratch(float** out) {
   }
   if (dev < 0 || dev >= kNoAllocDevices) return GPO_NO_DEVICE;
   std::lock_guard<std::mutex> lk(g_noalloc_mu);
-  if (!g_noalloc_ptr[dev]) {
+  NoAllocSlot& slot = g_noalloc[dev];
+  void* ctx = current_context();
+  if (slot.ptr == nullptr || ctx == nullptr || ctx != slot.ctx) {
     void* p = nullptr;
     const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_partials);
     if (e != cudaSuccess || !p) {
       cudaGetLastError();
       return GPO_LAUNCH_ERROR;
     }
-    g_noalloc_ptr[dev] = static_cast<float*>(p);
+    slot.ptr = static_cast<float*>(p);
+    slot.ctx = current_context();  // current now, if it was not before
   }
-  *out = g_noalloc_ptr[dev];
+  *out = slot.ptr;
   return GPO_OK;
 }
 

@@ -530,11 +530,20 @@ __device__ __forceinline__ float2 block_allreduce_sum2(float2 v, float2* red2) {
 // and takes the row statistics in one pass: sums of d = x - x0 and d^2
 // with x0 the row's first element (the shifted-data variance, exact in
 // real arithmetic and free of the E[x^2] - E[x]^2 cancellation as long as
-// x0 lies within a few standard deviations of the mean, which a sample of
-// the row does), so each row needs one block reduction of two values
-// instead of the two dependent reductions of the two-pass form; the math
-// runs on packed fp32x2 instructions.
+// x0 lies within a few standard deviations of the mean), so a row needs
+// one block reduction of two values instead of the two dependent
+// reductions of the centred form.  When the shift is far from the mean,
+// (mean - x0)^2 > kShiftGuard * var, the shifted variance has lost up to
+// kShiftGuard + 1 times fp32 rounding of its value, so the row takes a
+// second reduction of e = x - mean and e^2 over the values still in
+// registers: the mean gains the small correction sum(e) / n and the
+// variance is the centred one, the reference's single-tile formula
+// (compiler/triton/kernels.py:148-159).  For rows of
+// i.i.d. values that is the chance that the first element lies four
+// standard deviations out (6e-5).  The math runs on packed fp32x2
+// instructions.
 constexpr int kRowRing = 4;
+constexpr float kShiftGuard = 16.0f;
 
 template <typename T, int VPT, bool LN>
 __global__ void __launch_bounds__(row_pipe_max_threads(VPT)) rows_ring(const T* __restrict__ x,
@@ -634,8 +643,39 @@ __global__ void __launch_bounds__(row_pipe_max_threads(VPT)) rows_ring(const T* 
       refill();
       const float inv_n = 1.0f / static_cast<float>(n);
       const float dm = sq.x * inv_n;  // mean of d
-      const float mean = x0 + dm;
-      const float var = fmaxf(fmaf(-dm, dm, sq.y * inv_n), 0.f);
+      float mean = x0 + dm;
+      float var = fmaxf(fmaf(-dm, dm, sq.y * inv_n), 0.f);
+      // x0 far from the row mean (an outlying first element): the shifted
+      // sums then cancel, so take the centred sum of squares over the row
+      // values still in registers.  The vote keeps the branch (and its
+      // block reduction) uniform even where the lanes' reduced sums differ
+      // in their last bit.
+      if (__syncthreads_or(dm * dm > kShiftGuard * var)) {
+        // sums of e = x - mean and e^2: the mean takes the (now small)
+        // correction sum(e) / n and the variance is the centred one
+        const float2 nm2 = make_float2(-mean, -mean);
+        float2 eacc[4], cacc[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) eacc[i] = cacc[i] = make_float2(0.f, 0.f);
+#pragma unroll
+        for (int j = 0; j < VPT; ++j) {
+          const bool in = (threadIdx.x + static_cast<int64_t>(j) * blockDim.x) * V < n;
+#pragma unroll
+          for (int u = 0; u < P; ++u) {
+            if (in) {
+              const float2 e = __fadd2_rn(xv[j * P + u], nm2);
+              eacc[(j * P + u) & 3] = __fadd2_rn(eacc[(j * P + u) & 3], e);
+              cacc[(j * P + u) & 3] = __ffma2_rn(e, e, cacc[(j * P + u) & 3]);
+            }
+          }
+        }
+        const float2 e2 = __fadd2_rn(__fadd2_rn(eacc[0], eacc[1]), __fadd2_rn(eacc[2], eacc[3]));
+        const float2 c2 = __fadd2_rn(__fadd2_rn(cacc[0], cacc[1]), __fadd2_rn(cacc[2], cacc[3]));
+        const float2 ec = block_allreduce_sum2(make_float2(e2.x + e2.y, c2.x + c2.y), red2);
+        const float de = ec.x * inv_n;
+        mean += de;
+        var = fmaxf(fmaf(-de, de, ec.y * inv_n), 0.f);
+      }
       const float rstd = 1.0f / sqrtf(var + eps);
       const float2 nmean = make_float2(-mean, -mean), rstd2 = make_float2(rstd, rstd);
 #pragma unroll

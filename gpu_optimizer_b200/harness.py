@@ -177,7 +177,8 @@ class CudaBenchmarkEngine:
 
     # ------------------------------------------------------------- inputs
     def inputs_and_reference(self, task: Task, shape, dtype: str):
-        key = (task.name, task.profile, tuple(shape), dtype, self.settings.seed)
+        key = (task.name, getattr(task, "profile", type(task).__module__), tuple(shape), dtype,
+               self.settings.seed)
         hit = self._cache.get(key)
         if hit is not None:
             self._cache.move_to_end(key)
@@ -225,6 +226,12 @@ class CudaBenchmarkEngine:
                                           for i in range(s.iterations)])
 
     def _roofline(self, task: Task, shape, dtype: str, median_ms: float):
+        if not hasattr(task, "roofline_work"):
+            # a task object of the reference's own registry: the same task
+            # of this package's registry knows the algorithmic work
+            from .tasks import get_task
+
+            task = get_task(task.name)
         work = task.roofline_work(shape, dtype)
         if task.roofline_bound == "tensor":
             ach = work / (median_ms * 1e-3) / 1e12

@@ -12,9 +12,11 @@ JIT replaced by the sm_100a kernel library ``libgpo.so`` (include/gpo.h):
   and resource overflow (shared memory, TMEM, register tile) raise
   ``KernelBuildError`` with the library's log (runner.py:52-72), which the
   harness records as ``compile_error``.
-* ``warm_compile`` runs the callable once and synchronises; any launch
-  failure or device-side timeout becomes ``KernelBuildError``
-  (runner.py:75-89).
+* ``warm_compile`` runs the callable once and synchronises; a launch
+  failure becomes ``KernelBuildError`` (runner.py:75-89).  A device-side
+  wait that timed out is not a compile failure: the callable is marked
+  failed and its next call raises ``RuntimeError``, which both harnesses
+  record as ``runtime_error`` (harness.py:182-184).
 * ``render_source`` returns the CUDA source of the kernel family plus the
   resolved configuration, without a GPU (runner.py:275-297).
 
@@ -63,6 +65,9 @@ class KernelCallable:
     description: str
     launch: dict = field(default_factory=dict)
     module: object = None
+    # set by warm_compile when the first run's device wait timed out; fn
+    # then raises instead of launching
+    state: dict = field(default_factory=dict)
 
 
 _TASK_INPUTS = {"matmul": 2, "vecadd": 2, "reduction": 1, "softmax": 1, "layernorm": 3,
@@ -124,9 +129,12 @@ def build_callable(task: str, shape: Sequence[int], config: Config,
     args.scale = 0.0
     args.eps = 0.0
     keep = (ins, out, scratch)  # keep buffers alive as long as fn
+    state: dict = {}
 
     def fn() -> torch.Tensor:
         _ = keep
+        if state.get("failed"):
+            raise RuntimeError(state["failed"])
         rc = mod.launch(args, torch.cuda.current_stream().cuda_stream)
         if rc != _lib.OK:
             raise RuntimeError(f"gpo_launch failed: {_lib.status_name(rc)}")
@@ -135,13 +143,15 @@ def build_callable(task: str, shape: Sequence[int], config: Config,
     launch = {"grid": res["grid"], "kernel": res["kernel"], "smem_bytes": res["smem_bytes"],
               "tmem_cols": res["tmem_cols"], "threads": res["threads_per_cta"],
               "launches_per_call": res["launches_per_call"], **config}
-    return KernelCallable(fn, f"b200 {res['kernel']}", launch, mod)
+    return KernelCallable(fn, f"b200 {res['kernel']}", launch, mod, state)
 
 
 def warm_compile(kc: KernelCallable) -> float:
     """Run once and synchronise; returns first-run seconds.
 
-    Launch failures and device-side wait timeouts raise KernelBuildError.
+    A launch failure raises KernelBuildError (compile_error).  A device-side
+    wait that timed out marks the callable failed instead, so that its next
+    call raises RuntimeError (runtime_error in the harness).
     """
     t0 = time.perf_counter()
     try:
@@ -149,7 +159,10 @@ def warm_compile(kc: KernelCallable) -> float:
         rc, flags = _lib.device_status(torch.cuda.current_stream().cuda_stream)
     except Exception as e:
         raise KernelBuildError(f"first launch failed: {e}", log=str(e)) from e
-    if rc != _lib.OK:
+    if rc == _lib.TIMEOUT:
+        kc.state["failed"] = (f"device wait timed out on the first launch "
+                              f"({_lib.status_name(rc)}, flags {flags:#x})")
+    elif rc != _lib.OK:
         raise KernelBuildError(f"first launch failed: {_lib.status_name(rc)} (flags {flags:#x})")
     return time.perf_counter() - t0
 

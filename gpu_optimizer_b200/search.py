@@ -42,6 +42,10 @@ class RewardConfig:
     memory_penalty: float = 0.5
     clip: float | None = 8.0
 
+    def __post_init__(self) -> None:
+        if self.mode not in ("speedup", "log_speedup"):
+            raise ValueError(f"unknown reward mode {self.mode!r}")
+
 
 def compute_reward(result: BenchmarkResult, baseline_ms: float,
                    cfg: RewardConfig | None = None) -> float:

@@ -3,10 +3,12 @@
 The search stack of the reference (searchers, action catalog, validity
 masks, surrogate) speaks in config dicts over per-task parameter spaces
 (compiler/transformations/space.py:23-206).  This module keeps that
-interface — same Config dict, same ordered-choice ParamSpec semantics, same
-``candidate_id`` (sha1 of the sorted JSON of task, shape and config,
-space.py:185-191) — so results recorded by this backend key into the
-reference's results database and searchers unchanged.
+interface — same Config dict, same ParamSpec semantics (ordered discrete
+choices, or a continuous [low, high] range), same ``candidate_id`` (sha1
+of the sorted JSON of task, shape and config, space.py:185-191) — so
+results recorded by this backend key into the reference's results database
+and searchers unchanged.  The agreement is tested against the reference's
+own module where it is installed.
 """
 
 from __future__ import annotations
@@ -24,15 +26,31 @@ Config = dict[str, ConfigValue]
 
 @dataclass(frozen=True)
 class ParamSpec:
-    """One tunable parameter with an ordered tuple of discrete choices."""
+    """One tunable parameter: an ordered tuple of discrete ``choices``
+    (adjacent entries are neighbours), or a continuous ``low``..``high``
+    range (space.py:26-58)."""
 
     name: str
-    choices: tuple[ConfigValue, ...]
+    choices: tuple[ConfigValue, ...] | None = None
+    low: float | None = None
+    high: float | None = None
+
+    def __post_init__(self) -> None:
+        if (self.choices is None) == (self.low is None or self.high is None):
+            raise ValueError(f"{self.name}: specify either choices or (low, high)")
+
+    @property
+    def is_continuous(self) -> bool:
+        return self.choices is None
 
     def sample(self, rng: random.Random) -> ConfigValue:
+        if self.is_continuous:
+            return rng.uniform(self.low, self.high)
         return rng.choice(self.choices)
 
     def index_of(self, value: ConfigValue) -> int:
+        if self.is_continuous:
+            raise TypeError(f"{self.name} is continuous")
         return self.choices.index(value)
 
 
@@ -54,9 +72,14 @@ class ParamSpace:
     def __contains__(self, name: str) -> bool:
         return name in self.specs
 
+    @property
+    def discrete_specs(self) -> list[ParamSpec]:
+        return [s for s in self if not s.is_continuous]
+
     def size(self) -> int:
+        """Number of discrete configurations (continuous parameters excluded)."""
         n = 1
-        for s in self:
+        for s in self.discrete_specs:
             n *= len(s.choices)
         return n
 
@@ -64,10 +87,17 @@ class ParamSpace:
         return {s.name: s.sample(rng) for s in self}
 
     def grid(self, limit: int | None = None) -> list[Config]:
-        names = [s.name for s in self]
+        """Cartesian product of the discrete parameters; continuous ones at
+        their midpoint."""
+        disc = self.discrete_specs
+        names = [s.name for s in disc]
         out: list[Config] = []
-        for combo in itertools.product(*(s.choices for s in self)):
-            out.append(dict(zip(names, combo)))
+        for combo in itertools.product(*(s.choices for s in disc)):
+            cfg: Config = dict(zip(names, combo))
+            for s in self:
+                if s.is_continuous:
+                    cfg[s.name] = (s.low + s.high) / 2.0
+            out.append(cfg)
             if limit is not None and len(out) >= limit:
                 break
         return out
@@ -76,12 +106,17 @@ class ParamSpace:
         for s in self:
             if s.name not in config:
                 raise ValueError(f"missing param {s.name}")
-            if config[s.name] not in s.choices:
-                raise ValueError(f"{s.name}={config[s.name]!r} not in {s.choices}")
+            v = config[s.name]
+            if s.is_continuous:
+                if not (s.low <= float(v) <= s.high):
+                    raise ValueError(f"{s.name}={v} outside [{s.low}, {s.high}]")
+            elif v not in s.choices:
+                raise ValueError(f"{s.name}={v!r} not in {s.choices}")
 
     def neighbors(self, config: Config) -> list[Config]:
+        """Configs one discrete step away (the local-mutation neighbourhood)."""
         out = []
-        for s in self:
+        for s in self.discrete_specs:
             idx = s.index_of(config[s.name])
             for d in (-1, 1):
                 j = idx + d
@@ -113,6 +148,10 @@ class Candidate:
     @property
     def dtype(self) -> str:
         return str(self.config.get("dtype", "float32"))
+
+    def mutated(self, config: Config, provenance: str) -> Candidate:
+        return Candidate(task=self.task, shape=self.shape, config=config,
+                         parent_id=self.candidate_id, provenance=provenance)
 
     def describe(self) -> str:
         cfg = ", ".join(f"{k}={v}" for k, v in sorted(self.config.items()))

@@ -53,10 +53,6 @@ DEFAULT_TOLERANCES: dict[str, tuple[float, float]] = {
     "bfloat16": (2e-2, 1e-2),
 }
 
-# Relative-error bounds of the B200 benchmark configurations, checked under
-# an |ref| > atol floor (a pure relative error is unbounded near zero).
-B200_REL_BOUND = {"float32": 1e-5, "tf32": 1e-2, "float16": 1e-2, "bfloat16": 1e-2}
-
 FUSED_SCALE = 0.7071  # benchmarks/fused_elementwise/task.py:19
 LN_EPS = 1e-5         # benchmarks/layernorm/task.py:15
 

@@ -45,8 +45,12 @@ extern "C" {
 #endif
 
 /* Status codes.  GPO_COMPILE_ERROR maps to the reference's compile_error
- * status (benchmarks/harness.py:34,169-173); GPO_LAUNCH_ERROR and
- * GPO_TIMEOUT map to runtime_error (benchmarks/harness.py:35,182-184). */
+ * status (benchmarks/harness.py:34,169-173).  GPO_LAUNCH_ERROR on a
+ * candidate's first launch (warm_compile) is compile_error too, as the
+ * reference's first-launch failures are (compiler/triton/runner.py:75-89);
+ * after it, runtime_error.  GPO_TIMEOUT is always runtime_error
+ * (benchmarks/harness.py:35,182-184): a wait that gave up says nothing about
+ * whether the candidate compiles. */
 typedef enum gpo_status {
   GPO_OK = 0,
   GPO_COMPILE_ERROR = 1, /* a real resource limit is exceeded; log says which */
@@ -171,15 +175,19 @@ GPO_API gpo_status gpo_selftest_timeout(void* stream, uint32_t limit_ms, uint32_
 /* Sum of n fp32 values with the two_pass algorithm (per-slice partial sums,
  * then one CTA summing the partials), without allocating anything: the
  * partial sums live in a fixed 65536-float array inside the library, so a
- * caller that cannot allocate device memory (inside a stream capture, under
- * a host runtime's fixed memory budget, or as a plug-in given only its input
- * and output buffers) passes just x (device, n floats), out (device, one
- * float), BLOCK_SIZE and num_warps.  Same kernels and numerics as the
- * two_pass strategy of gpo_launch.
+ * caller that cannot allocate device memory passes just x (device, n
+ * floats), out (device, one float), BLOCK_SIZE and num_warps.  Such callers
+ * are plug-in hosts that own all device memory and give a kernel library
+ * only its input and output buffers (an allocation escapes the host's
+ * accounting and can fail under its memory cap), and latency-critical
+ * callers that cannot accept the device synchronisation a cudaMalloc /
+ * cudaFree pair can cause.  Same kernels and numerics as the two_pass
+ * strategy of gpo_launch.
  *  - Limit: cdiv(n, block_size) <= 65536, i.e. n <= 65536 * block_size;
  *    larger n returns GPO_BAD_ARGS before anything is launched.
- *  - The first call on a device looks up the array's device address; make
- *    that first call before any stream capture.
+ *  - The first call on a device (and the first after that device's context
+ *    is recreated, e.g. by cudaDeviceReset) looks up the array's device
+ *    address; make that first call before any stream capture.
  *  - All calls on a device share the array: calls whose kernels may overlap
  *    on the GPU (unordered streams) race; calls on one stream do not.
  *  - No cudaMalloc, cudaFree or other allocation is made by this call.

@@ -1,8 +1,8 @@
 """Generate the golden fixtures by running the reference's own code.
 
-Run in the build container, where the reference checkout is readable:
+Run where a checkout of the reference is readable, giving its path:
 
-    PYTHONDONTWRITEBYTECODE=1 python tests/golden/make_golden.py /root/reference
+    PYTHONDONTWRITEBYTECODE=1 python tests/golden/make_golden.py <reference checkout>
 
 For every reference task at the reference's odd-sized test shapes
 (tests/test_tasks_and_emulation.py:13-21) and each supported dtype, this
@@ -98,4 +98,6 @@ def main(ref_root: str) -> None:
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    if len(sys.argv) != 2:
+        sys.exit("usage: make_golden.py <path of the reference checkout>")
+    main(sys.argv[1])

@@ -107,3 +107,44 @@ def _rank_main(rank, world, port):
 
 def test_gloo_world_size_two_sharding():
     tmp.spawn(_rank_main, args=(2, _free_port()), nprocs=2, join=True)
+
+
+def _slow_square(item):
+    import time
+
+    time.sleep(item[1])
+    return item[0] * item[0]
+
+
+def _pull_main(rank, world, port):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        # one long item and many short ones: the rank that draws the long one
+        # takes few others, so both finish near the same time
+        items = [(i, 0.6 if i == 3 else 0.05) for i in range(14)]
+        order = sorted(range(len(items)), key=lambda i: -items[i][1])  # longest first
+        out, st = D.pull_partition(items, _slow_square, order)
+        assert out == [i * i for i in range(14)]
+        ranks = st["ranks"]
+        assert [r["rank"] for r in ranks] == list(range(world))
+        assert sum(r["count"] for r in ranks) == len(items)
+        assert all(r["count"] >= 1 for r in ranks)
+        long_rank = 0 if ranks[0]["busy_s"] > ranks[1]["busy_s"] else 1
+        assert ranks[long_rank]["count"] < ranks[1 - long_rank]["count"]
+        # a second batch on the same group uses a fresh counter
+        out2, _ = D.pull_partition([(i, 0.0) for i in range(5)], _slow_square)
+        assert out2 == [i * i for i in range(5)]
+        D.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+def test_gloo_world_size_two_pull_partition():
+    """The search batch is split by a shared counter in the group's store."""
+    tmp.spawn(_pull_main, args=(2, _free_port()), nprocs=2, join=True)
+
+
+def test_pull_partition_without_a_group():
+    out, st = D.pull_partition([(2, 0.0), (3, 0.0)], _slow_square, [1, 0])
+    assert out == [4, 9] and st["ranks"][0]["count"] == 2

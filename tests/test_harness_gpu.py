@@ -155,3 +155,31 @@ def test_multi_device_evaluator_on_gpu():
     assert [r.candidate_id for r in res] == [c.candidate_id for c in cands]
     assert all(r.status in ("ok", "compile_error") for r in res), [r.error for r in res]
     assert any(r.status == "ok" for r in res)
+
+
+def test_device_timeout_on_first_launch_is_a_runtime_error(monkeypatch):
+    """GPO_TIMEOUT maps to runtime_error end to end: a first launch whose
+    bounded device wait gave up is not a compile failure (the surrogate's
+    P(compile) label stays clean), and the candidate's later calls raise."""
+    from gpu_optimizer_b200 import _lib
+
+    real = _lib.device_status
+    calls = {"n": 0}
+
+    def timed_out_once(stream):
+        calls["n"] += 1
+        if calls["n"] == 1:
+            real(stream)  # synchronise as the real call does
+            return _lib.TIMEOUT, 1 << 6
+        return real(stream)
+
+    monkeypatch.setattr(_lib, "device_status", timed_out_once)
+    eng = CudaBenchmarkEngine(settings=BenchmarkSettings(warmup=1, iterations=2))
+    task = get_task("vecadd", "b200")
+    cand = task.make_candidate((1 << 16,), {"BLOCK_SIZE": 1024, "num_warps": 4,
+                                            "dtype": "float32"})
+    res = eng.benchmark_candidate(task, cand)
+    assert res.status == "runtime_error", (res.status, res.error)
+    assert "timed out" in res.error
+    # the next candidate on the same engine is unaffected
+    assert eng.benchmark_candidate(task, cand).status == "ok"

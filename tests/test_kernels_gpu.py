@@ -191,17 +191,16 @@ def test_tcgen05_attention_shapes(shape, dtype, causal):
     # tiles on M=64 MMAs
     for bm, bn, stages, warps in [(bm, bn, st, w) for bm in (64, 128, 256) for bn in (32, 64, 128)
                                   for st in (1, 2, 3) for w in (4, 8)]:
-        if True:
-            cfg = {"BLOCK_M": bm, "BLOCK_N": bn, "num_warps": warps, "num_stages": stages,
-                   "dtype": dtype}
-            try:
-                out, kc = run(name, shape, cfg, inputs)
-            except KernelBuildError as e:
-                assert "GPO_COMPILE_ERROR" in str(e), f"{cfg}: {e}"
-                continue
-            assert kc.launch["kernel"].startswith("attn_tc_kernel")
-            assert_close(name, dtype, out, ref, f"{shape} {cfg}")
-            ran += 1
+        cfg = {"BLOCK_M": bm, "BLOCK_N": bn, "num_warps": warps, "num_stages": stages,
+               "dtype": dtype}
+        try:
+            out, kc = run(name, shape, cfg, inputs)
+        except KernelBuildError as e:
+            assert "GPO_COMPILE_ERROR" in str(e), f"{cfg}: {e}"
+            continue
+        assert kc.launch["kernel"].startswith("attn_tc_kernel")
+        assert_close(name, dtype, out, ref, f"{shape} {cfg}")
+        ran += 1
     assert ran >= 9
 
 

@@ -1,6 +1,7 @@
 """gpo_reduction_sum_noalloc: the two_pass sum for callers that cannot
-allocate device memory (inside a stream capture, under a host runtime's
-fixed memory budget, or as a plug-in handed only input and output buffers).
+allocate device memory (plug-in hosts that own all device memory and hand
+a kernel library only its input and output buffers; latency-critical
+callers that cannot take the device synchronisation of cudaMalloc/cudaFree).
 
 It is checked through the C-ABI against the existing two_pass strategy of
 gpo_launch (which uses a caller-allocated partial-sum buffer) on two calls
