@@ -476,21 +476,6 @@ SEARCH_SHAPE = (4096, 4096, 4096)
 SEARCH_BATCH = 128
 
 
-def _search_cost(cand) -> float:
-    """Relative cost of one candidate for the longest-first dispatch order:
-    CUDA-core tiles are the slow ones; compile errors cost nothing (the
-    planner refuses them on the host)."""
-    from gpu_optimizer_b200.runner import KernelBuildError, compile_module
-
-    try:
-        kernel = compile_module("matmul", cand.shape, cand.config).resources()["kernel"]
-    except KernelBuildError:
-        return 0.0
-    if "simt" in kernel:
-        return 30.0
-    return 3.0 if cand.config.get("dtype") == "tf32" else 1.0
-
-
 def run_search(world, rank):
     """Search throughput: candidates evaluated per second for ONE batch of the
     B200 matmul space at 4096^3 -- 128 distinct candidates drawn once from a
@@ -507,6 +492,7 @@ def run_search(world, rank):
     import random
 
     from gpu_optimizer_b200 import distributed as D
+    from gpu_optimizer_b200.dispatch import longest_first
     from gpu_optimizer_b200.harness import BenchmarkSettings, CudaBenchmarkEngine
     from gpu_optimizer_b200.tasks import get_task
 
@@ -525,7 +511,7 @@ def run_search(world, rank):
     for dt in space["dtype"].choices:
         eng.inputs_and_reference(task, SEARCH_SHAPE, dt)
     torch.cuda.synchronize()
-    order = sorted(range(len(cands)), key=lambda i: -_search_cost(cands[i]))
+    order = longest_first(cands)
     results, st = D.pull_partition(cands, lambda c: eng.benchmark_candidate(task, c), order)
     ranks = st["ranks"]
     wall = max(r["wall_s"] for r in ranks)

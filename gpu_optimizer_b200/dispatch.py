@@ -32,6 +32,28 @@ from .space import Candidate
 EngineFactory = Callable[[int, BenchmarkSettings, int], object]
 
 
+def relative_cost(cand: Candidate) -> float:
+    """Relative evaluation cost of a candidate, from the host-side plan:
+    CUDA-core tiles run longest, tf32 tensor-core tiles next, 16-bit ones
+    least; a candidate the planner refuses costs nothing (compile_error)."""
+    from .runner import KernelBuildError, compile_module
+
+    try:
+        kernel = compile_module(cand.task, cand.shape, cand.config).resources()["kernel"]
+    except KernelBuildError:
+        return 0.0
+    if "simt" in kernel:
+        return 30.0
+    return 3.0 if cand.config.get("dtype") == "tf32" else 1.0
+
+
+def longest_first(candidates: Sequence[Candidate]) -> list[int]:
+    """Dispatch order for a partitioned batch: most expensive first, so
+    that the devices finish together (longest-processing-time order)."""
+    costs = [relative_cost(c) for c in candidates]
+    return sorted(range(len(candidates)), key=lambda i: -costs[i])
+
+
 def cuda_engine_factory(device: int, settings: BenchmarkSettings, worker_id: int):
     """Default factory: a CudaBenchmarkEngine on the (only) visible device."""
     from .harness import CudaBenchmarkEngine
@@ -162,16 +184,23 @@ class MultiDeviceEvaluator:
                     self._replace(w)
         return all(w.ready for w in self._workers)
 
-    def evaluate(self, candidates: Sequence[Candidate]) -> list[BenchmarkResult]:
+    def evaluate(self, candidates: Sequence[Candidate],
+                 order: Sequence[int] | None = None) -> list[BenchmarkResult]:
         """Results in the order of ``candidates``.
 
-        A candidate's deadline starts when a ready worker receives it; a
-        worker that exits or misses the deadline is replaced and its
-        candidate recorded as runtime_error.
+        ``order`` is the dispatch order (indices into ``candidates``,
+        default the proposal order); handing out the longest candidates
+        first lets the devices finish together.  A candidate's deadline
+        starts when a ready worker receives it; a worker that exits or
+        misses the deadline is replaced and its candidate recorded as
+        runtime_error.
         """
         n = len(candidates)
         results: list[BenchmarkResult | None] = [None] * n
-        todo = list(range(n))[::-1]
+        order = list(range(n)) if order is None else list(order)
+        if sorted(order) != list(range(n)):
+            raise ValueError("order must be a permutation of the candidate indices")
+        todo = order[::-1]
         done = 0
         respawn_budget = 10 * len(self._workers) + n
 

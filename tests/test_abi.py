@@ -101,6 +101,20 @@ def test_attention_plans():
                         {**base, "BLOCK_M": 256, "num_stages": 4}).resources()
     assert r5["kernel"].endswith("sbufs=3,cta_pair>") and r5["grid"] == [32, 128, 1]
     assert r5["threads_per_cta"] == 256 and r5["tmem_cols"] == 512
+    # BLOCK_M 256 with 8 warps: two query tiles per CTA, one softmax
+    # warpgroup each (O 2 x 128 + S 2 x 128 columns = all of TMEM)
+    rd = compile_module("attention_causal", (128, 4096, 128),
+                        {**base, "BLOCK_M": 256, "num_warps": 8}).resources()
+    assert rd["kernel"] == "attn_tc_dual_kernel<bf16,BN=128,D=128,causal,two_tiles>"
+    assert rd["grid"] == [16, 128, 1] and rd["threads_per_cta"] == 384
+    assert rd["tmem_cols"] == 512 and rd["smem_bytes"] <= 227 * 1024
+    for bad in ({"num_stages": 3}, {"BLOCK_N": 128, "num_stages": 4}):  # shared memory
+        with pytest.raises(KernelBuildError, match="shared memory"):
+            compile_module("attention", (128, 4096, 128),
+                           {**base, "BLOCK_M": 256, "num_warps": 8, **bad})
+    with pytest.raises(KernelBuildError, match="TMEM"):  # 2 x 256 + 2 x 32 columns
+        compile_module("attention", (4, 512, 256),
+                       {**base, "BLOCK_M": 256, "BLOCK_N": 32, "num_warps": 8})
     # BLOCK_N 64 (D 128), one warpgroup, two stages: two S/P buffers keep the
     # CTA within 256 TMEM columns so that two CTAs share an SM
     r6 = compile_module("attention", (128, 4096, 128), {**base, "BLOCK_N": 64}).resources()

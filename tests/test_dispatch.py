@@ -31,7 +31,13 @@ def test_results_come_back_in_proposal_order():
         assert ev.wait_ready(120)
         cs = cands(["ok"] * 17)
         res = ev.evaluate(cs)
+        # a dispatch order (longest first) changes who runs what, not the
+        # order of the results
+        res2 = ev.evaluate(cs, order=list(range(17))[::-1])
+        with pytest.raises(ValueError):
+            ev.evaluate(cs, order=[0, 0])
     assert [r.candidate_id for r in res] == [c.candidate_id for c in cs]
+    assert [r.candidate_id for r in res2] == [c.candidate_id for c in cs]
     assert all(r.status == "ok" for r in res)
     assert len({r.worker_id for r in res}) > 1  # work was spread
 
@@ -148,3 +154,17 @@ def test_gloo_world_size_two_pull_partition():
 def test_pull_partition_without_a_group():
     out, st = D.pull_partition([(2, 0.0), (3, 0.0)], _slow_square, [1, 0])
     assert out == [4, 9] and st["ranks"][0]["count"] == 2
+
+
+def test_longest_first_order_from_the_plan():
+    from gpu_optimizer_b200.dispatch import longest_first, relative_cost
+
+    shape = (4096, 4096, 4096)
+    base = {"BLOCK_K": 64, "GROUP_M": 8, "num_warps": 8, "num_stages": 3}
+    tc = Candidate("matmul", shape, {**base, "BLOCK_M": 128, "BLOCK_N": 256, "dtype": "bfloat16"})
+    refused = Candidate("matmul", shape, {**base, "BLOCK_M": 256, "BLOCK_N": 256,
+                                          "BLOCK_K": 128, "num_stages": 6, "dtype": "bfloat16"})
+    simt = Candidate("matmul", shape, {**base, "BLOCK_M": 64, "BLOCK_N": 64, "dtype": "float32"})
+    tf32 = Candidate("matmul", shape, {**base, "BLOCK_M": 128, "BLOCK_N": 128, "dtype": "tf32"})
+    assert relative_cost(refused) == 0.0
+    assert longest_first([tc, refused, simt, tf32]) == [2, 3, 0, 1]
