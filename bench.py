@@ -435,9 +435,10 @@ EXTRA_TASKS = [
                                "dtype": "float32"}),
     ("fused_gelu", (1 << 26,), {"BLOCK_SIZE": 4096, "num_warps": 4, "strategy": "fused",
                                 "dtype": "bfloat16"}),
-    ("attention_causal", (128, 4096, 128), {"BLOCK_M": 128, "BLOCK_N": 128, "num_warps": 4,
+    # two query tiles per CTA (BLOCK_M 256, 8 softmax warps)
+    ("attention_causal", (128, 4096, 128), {"BLOCK_M": 256, "BLOCK_N": 128, "num_warps": 8,
                                             "num_stages": 2, "dtype": "bfloat16"}),
-    ("attention", (128, 4096, 128), {"BLOCK_M": 128, "BLOCK_N": 128, "num_warps": 4,
+    ("attention", (128, 4096, 128), {"BLOCK_M": 256, "BLOCK_N": 128, "num_warps": 8,
                                      "num_stages": 2, "dtype": "bfloat16"}),
     ("matmul", (8192, 8192, 8192), {"BLOCK_M": 256, "BLOCK_N": 256, "BLOCK_K": 128,
                                     "GROUP_M": 16, "num_warps": 8, "num_stages": 3,

@@ -554,7 +554,7 @@ struct AttnDualShared {
   uint64_t v_full[kAttnMaxStages];
   uint64_t v_empty[kAttnMaxStages];
   uint64_t s_full[2];
-  uint64_t p_full[2];
+  uint64_t p_full[2][2];  // [tile][half of the block's keys]
   uint64_t pv_done[2];
   uint64_t drain;
   uint32_t tmem_base;
@@ -646,7 +646,10 @@ __device__ __forceinline__ void attn_dual_mma(AttnDualShared& sh, uint32_t tmem,
   constexpr uint32_t KV_SLOT = ((static_cast<uint32_t>(BN) * D * G::ES) + 1023u) & ~1023u;
   constexpr uint32_t IDESC_S = make_idesc(FMT, 128, BN, false, false);
   constexpr uint32_t IDESC_O = make_idesc(FMT, 128, D, false, true);
-  bool ok = mbar_wait(smem_u32(&sh.q_full), 0, abort_flag, err, kErrWaitMma);
+  auto wait = [&](const uint64_t* bar, uint32_t parity) {
+    return mbar_wait(smem_u32(bar), parity, abort_flag, err, kErrWaitMma);
+  };
+  bool ok = wait(&sh.q_full, 0);
   auto s_mma = [&](int t, int j) {
     const uint32_t ks = k_smem + static_cast<uint32_t>(j % stages) * KV_SLOT;
     const uint32_t qs = q_smem + static_cast<uint32_t>(t) * G::Q_BYTES;
@@ -662,29 +665,34 @@ __device__ __forceinline__ void attn_dual_mma(AttnDualShared& sh, uint32_t tmem,
     mma_commit(smem_u32(&sh.s_full[t]));
   };
   // P_t sits in the first BN/2 columns of tile t's S/P buffer
-  auto pv_mma = [&](int t, int j) {
+  auto pv_mma = [&](int t, int j, bool last) {
     const uint32_t vs = v_smem + static_cast<uint32_t>(j % stages) * KV_SLOT;
     const uint32_t pa = tmem + static_cast<uint32_t>(2 * D + t * BN);
     const uint32_t o_tmem = tmem + static_cast<uint32_t>(t * D);
+    // keys [0, BN/2) as soon as their P is stored, then the rest
 #pragma unroll
-    for (int kk = 0; kk < BN / 16; ++kk) {
-      const uint64_t bdesc = make_smem_desc(vs + kk * 16 * SW, BN * SW, 8 * SW, SW);
-      mma_f16_ts(o_tmem, pa + static_cast<uint32_t>(kk * 8), bdesc, IDESC_O,
-                 (j > 0 || kk > 0) ? 1u : 0u);
+    for (int h = 0; h < 2; ++h) {
+      if (!wait(&sh.p_full[t][h], static_cast<uint32_t>(j) & 1u)) return false;
+      tc_fence_after();
+#pragma unroll
+      for (int kk = h * (BN / 32); kk < (h + 1) * (BN / 32); ++kk) {
+        const uint64_t bdesc = make_smem_desc(vs + kk * 16 * SW, BN * SW, 8 * SW, SW);
+        mma_f16_ts(o_tmem, pa + static_cast<uint32_t>(kk * 8), bdesc, IDESC_O,
+                   (j > 0 || kk > 0) ? 1u : 0u);
+      }
     }
-    mma_commit(smem_u32(&sh.pv_done[t]));
+    if (last) mma_commit(smem_u32(&sh.pv_done[t]));  // for the epilogue
+    return true;
   };
-  if (ok) ok = mbar_wait(smem_u32(&sh.k_full[0]), 0, abort_flag, err, kErrWaitMma);
+  if (ok) ok = wait(&sh.k_full[0], 0);
   if (ok) {
     tc_fence_after();
     s_mma(0, 0);
     s_mma(1, 0);
-    mma_commit(smem_u32(&sh.k_empty[0]));
   }
   for (int j = 0; j < nb1 && ok; ++j) {
     const int sv = j % stages;
-    if (!mbar_wait(smem_u32(&sh.v_full[sv]), static_cast<uint32_t>(j / stages) & 1u, abort_flag,
-                   err, kErrWaitMma)) {
+    if (!wait(&sh.v_full[sv], static_cast<uint32_t>(j / stages) & 1u)) {
       ok = false;
       break;
     }
@@ -692,28 +700,17 @@ __device__ __forceinline__ void attn_dual_mma(AttnDualShared& sh, uint32_t tmem,
 #pragma unroll
     for (int t = 0; t < 2; ++t) {
       const int nbt = t == 0 ? nb0 : nb1;
-      if (ok && j < nbt) {
-        ok = mbar_wait(smem_u32(&sh.p_full[t]), static_cast<uint32_t>(j) & 1u, abort_flag, err,
-                       kErrWaitMma);
-        if (ok) {
-          tc_fence_after();
-          pv_mma(t, j);
-        }
-      }
+      if (ok && j < nbt) ok = pv_mma(t, j, j + 1 == nbt);
       if (ok && j + 1 < nbt) {
         if (!k_ready) {
           const int sk = (j + 1) % stages;
-          ok = mbar_wait(smem_u32(&sh.k_full[sk]), static_cast<uint32_t>((j + 1) / stages) & 1u,
-                         abort_flag, err, kErrWaitMma);
+          ok = wait(&sh.k_full[sk], static_cast<uint32_t>((j + 1) / stages) & 1u);
           tc_fence_after();
           k_ready = true;
         }
         if (ok) s_mma(t, j + 1);
       }
     }
-    if (!ok) break;
-    mma_commit(smem_u32(&sh.v_empty[sv]));
-    if (j + 1 < nb1) mma_commit(smem_u32(&sh.k_empty[(j + 1) % stages]));
   }
   if (!ok) {
     mma_commit(smem_u32(&sh.drain));
@@ -726,8 +723,8 @@ __device__ __forceinline__ void attn_dual_mma(AttnDualShared& sh, uint32_t tmem,
 template <typename T, int FMT, int BN, int D, bool CAUSAL>
 __device__ __forceinline__ void attn_dual_softmax(AttnDualShared& sh, uint32_t tmem,
                                                   T* __restrict__ O, int S, int q0, int bh,
-                                                  int nb0, int nb1, float scale_log2, int warp,
-                                                  int lane, volatile int* abort_flag,
+                                                  int nb0, int nb1, int stages, float scale_log2,
+                                                  int warp, int lane, volatile int* abort_flag,
                                                   unsigned int* err) {
   const int t = (warp - 4) >> 2;
   const int q = warp & 3;  // TMEM lane quarter
@@ -751,6 +748,15 @@ __device__ __forceinline__ void attn_dual_softmax(AttnDualShared& sh, uint32_t t
       break;
     }
     tc_fence_after();
+    // MMAs complete in issue order, so S_1(j) done means every MMA before
+    // it is done: S_0(j) and S_1(j), the last readers of K(j), and the PV
+    // MMAs of block j - 1, the last readers of V(j - 1).  Tile 1 (which
+    // has every block of the span) hands both ring slots back here, with
+    // no commit on the MMA thread.
+    if (t == 1 && q == 0 && lane == 0) {
+      mbar_arrive(smem_u32(&sh.k_empty[j % stages]));
+      if (j > 0) mbar_arrive(smem_u32(&sh.v_empty[(j - 1) % stages]));
+    }
     uint32_t sv[BN];
 #pragma unroll
     for (int c = 0; c < BN / 32; ++c)
@@ -776,14 +782,8 @@ __device__ __forceinline__ void attn_dual_softmax(AttnDualShared& sh, uint32_t t
       if (__any_sync(0xffffffffu, need)) {
         const float m_new = need ? mb : m_used;
         const float alpha = ex2_approx(m_used - m_new);
-        // O_t holds PV_t(0..j-1); wait for PV_t(j-1) before rescaling it
-        ok = mbar_wait(smem_u32(&sh.pv_done[t]), static_cast<uint32_t>(j - 1) & 1u, abort_flag,
-                       err, kErrWaitSoftmax);
-        if (!__all_sync(0xffffffffu, ok)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
+        // O_t holds PV_t(0..j-1), complete: PV_t(j-1) was issued before
+        // S_t(j), which is done, and PV_t(j) waits for this thread's P
 #pragma unroll 1
         for (int c = 0; c < D / 16; ++c) {
           uint32_t r[16];
@@ -804,7 +804,16 @@ __device__ __forceinline__ void attn_dual_softmax(AttnDualShared& sh, uint32_t t
     float2 rs[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f),
                     make_float2(0.f, 0.f)};
     // P_t(j) over the first BN/2 columns of the buffer, 16 columns as soon
-    // as they are packed
+    // as they are packed; the keys of each half of the block are released
+    // to the PV MMA as soon as their P is stored, so the MMA on the first
+    // half overlaps the exponentials of the second
+    auto release = [&](int h) {
+      tmem_wait_st();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_u32(&sh.p_full[t][h]));
+    };
+    constexpr int HALF_CHUNKS = BN / 64;  // 32-key chunks per half (0: BN 32)
 #pragma unroll
     for (int c = 0; c < BN / 32; ++c) {
       uint32_t pk[16];
@@ -817,18 +826,17 @@ __device__ __forceinline__ void attn_dual_softmax(AttnDualShared& sh, uint32_t t
         pk[g2] = FMT == 1 ? pack_bf16(p.x, p.y) : pack_f16(p.x, p.y);
       }
       tmem_st16(sp + static_cast<uint32_t>(c * 16), pk);
+      if (c + 1 == HALF_CHUNKS) release(0);
     }
     const float2 rsum = __fadd2_rn(__fadd2_rn(rs[0], rs[1]), __fadd2_rn(rs[2], rs[3]));
     l += rsum.x + rsum.y;
-    tmem_wait_st();
-    tc_fence_before();
-    __syncwarp();
-    if (lane == 0) mbar_arrive(smem_u32(&sh.p_full[t]));
+    if (HALF_CHUNKS == 0) release(0);
+    release(1);
   }
   // ------------------------------------------------------------ epilogue
+  // pv_done[t] is committed once, after the tile's last PV MMA
   if (ok && nblk > 0)
-    ok = mbar_wait(smem_u32(&sh.pv_done[t]), static_cast<uint32_t>(nblk - 1) & 1u, abort_flag,
-                   err, kErrWaitSoftmax);
+    ok = mbar_wait(smem_u32(&sh.pv_done[t]), 0u, abort_flag, err, kErrWaitSoftmax);
   if (__all_sync(0xffffffffu, ok)) {
     tc_fence_after();
     const float inv_l = l > 0.f ? 1.0f / l : 0.f;
@@ -897,7 +905,8 @@ __global__ void __launch_bounds__(kAttnDualThreads, 1)
     }
     for (int t = 0; t < 2; ++t) {
       mbar_init(smem_u32(&sh.s_full[t]), 1);
-      mbar_init(smem_u32(&sh.p_full[t]), 4);
+      mbar_init(smem_u32(&sh.p_full[t][0]), 4);
+      mbar_init(smem_u32(&sh.p_full[t][1]), 4);
       mbar_init(smem_u32(&sh.pv_done[t]), 1);
     }
     mbar_init(smem_u32(&sh.drain), 1);
@@ -929,8 +938,8 @@ __global__ void __launch_bounds__(kAttnDualThreads, 1)
                                 err);
   } else {
     regs_inc<kAttnDualHighRegs>();
-    attn_dual_softmax<T, FMT, BN, D, CAUSAL>(sh, tmem, O, S, q0, bh, nb0, nb1, scale_log2, warp,
-                                             lane, abort_flag, err);
+    attn_dual_softmax<T, FMT, BN, D, CAUSAL>(sh, tmem, O, S, q0, bh, nb0, nb1, stages,
+                                             scale_log2, warp, lane, abort_flag, err);
   }
   tc_fence_before();
   __syncthreads();

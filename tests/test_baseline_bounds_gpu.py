@@ -49,6 +49,10 @@ CASES = [
                                             "num_stages": 2, "dtype": "bfloat16"}),
     ("attention_causal", (128, 4096, 128), {"BLOCK_M": 128, "BLOCK_N": 128, "num_warps": 4,
                                             "num_stages": 2, "dtype": "float16"}),
+    ("attention", (128, 4096, 128), {"BLOCK_M": 256, "BLOCK_N": 128, "num_warps": 8,
+                                     "num_stages": 2, "dtype": "bfloat16"}),
+    ("attention_causal", (128, 4096, 128), {"BLOCK_M": 256, "BLOCK_N": 128, "num_warps": 8,
+                                            "num_stages": 2, "dtype": "bfloat16"}),
 ]
 
 
