@@ -35,7 +35,13 @@ EngineFactory = Callable[[int, BenchmarkSettings, int], object]
 def relative_cost(cand: Candidate) -> float:
     """Relative evaluation cost of a candidate, from the host-side plan:
     CUDA-core tiles run longest, tf32 tensor-core tiles next, 16-bit ones
-    least; a candidate the planner refuses costs nothing (compile_error)."""
+    least; a candidate the planner refuses costs nothing (compile_error).
+    A CUDA-core tile of a x b outputs per thread does a*b FMAs per a + b
+    operands it reads from shared memory, so its time per FLOP scales as
+    (a + b) / (a * b); the register-prefetch form (no cp.async pipeline)
+    is slower again."""
+    import re
+
     from .runner import KernelBuildError, compile_module
 
     try:
@@ -43,7 +49,10 @@ def relative_cost(cand: Candidate) -> float:
     except KernelBuildError:
         return 0.0
     if "simt" in kernel:
-        return 30.0
+        m = re.search(r"<(\d+)x(\d+) per thread>", kernel)
+        a, b = (int(m.group(1)), int(m.group(2))) if m else (8, 8)
+        cost = 120.0 * (a + b) / (a * b)  # 30 for an 8 x 8 tile
+        return cost if "async" in kernel else 1.3 * cost
     return 3.0 if cand.config.get("dtype") == "tf32" else 1.0
 
 
