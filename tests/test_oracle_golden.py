@@ -104,3 +104,66 @@ def test_oracle_gelu_matches_torch():
     z = ins[0] * O.FUSED_SCALE + ins[1]
     want = 0.5 * z * (1.0 + torch.erf(z / 2.0 ** 0.5))
     assert torch.allclose(ref, want, rtol=1e-5, atol=1e-6)
+
+
+def _causal_float64(q, k, v):
+    """Causal attention in float64 with numpy: an implementation that shares
+    no code with torch or with the oracle."""
+    qd, kd, vd = (t.double().numpy() for t in (q, k, v))
+    bh, s, d = qd.shape
+    sc = np.einsum("bqd,bkd->bqk", qd, kd) / np.sqrt(d)
+    sc = np.where(np.triu(np.ones((s, s), dtype=bool), 1)[None], -np.inf, sc)
+    sc = sc - sc.max(axis=-1, keepdims=True)
+    p = np.exp(sc)
+    p /= p.sum(axis=-1, keepdims=True)
+    return torch.from_numpy(np.einsum("bqk,bkd->bqd", p, vd))
+
+
+@pytest.mark.parametrize("dtype", ["float32", "float16", "bfloat16"])
+@pytest.mark.parametrize("shape", [(3, 130, 32), (1, 1024, 128)], ids=str)
+def test_causal_oracle_pinned_to_independent_implementations(shape, dtype):
+    """The causal attention oracle, on the reference's seeded inputs (the
+    inputs the golden index hashes for the attention task), agrees with
+    torch's own causal kernel (scaled_dot_product_attention, is_causal=True,
+    fp32 math on the CPU) to one rounding of the output, and with a float64
+    numpy computation to fp32 accuracy before that rounding."""
+    ins = O.make_inputs("attention_causal", shape, dtype, 0)
+    if shape == tuple(INDEX["tasks"]["attention"]["shape"]) and dtype != "float16":
+        for c in INDEX["tasks"]["attention"]["cases"]:
+            if c["dtype"] == dtype and c["seed"] == 0:
+                assert [sha(t) for t in ins] == c["input_sha"]
+    ref = O.reference("attention_causal", ins)
+    q, k, v = (t.float() for t in ins)
+    sdpa = torch.nn.functional.scaled_dot_product_attention(q, k, v, is_causal=True)
+    exact = _causal_float64(*ins)
+    ulp = {"float32": 2.0 ** -23, "float16": 2.0 ** -10, "bfloat16": 2.0 ** -7}[dtype]
+    mag = exact.abs().clamp_min(1e-3)
+    # fp32: two fp32 summation orders (measured 2e-6 relative); 16-bit: one
+    # output rounding apart at most
+    to_sdpa = (ref.double() - sdpa.to(ref.dtype).double()).abs()
+    bound = 1e-5 * mag + 1e-6 if dtype == "float32" else 1.01 * ulp * mag + 1e-6
+    assert (to_sdpa <= bound).all(), float(to_sdpa.max())
+    # against float64: half an output rounding plus fp32 noise
+    assert ((ref.double() - exact).abs() <= 0.51 * ulp * mag + 2e-6).all()
+
+
+def test_gelu_oracle_pinned_to_math_erf():
+    """The fused gelu oracle against Python's math.erf in float64 (no torch
+    in the loop), on the reference's seeded inputs of the elementwise task:
+    within four fp32 units of the result plus 1e-6 absolute: in fp32 the
+    formula 0.5 z (1 + erf(z / sqrt 2)) cancels in the negative tail (at
+    z = -2.7, 1 + erf is 0.007 and carries erf's absolute rounding), which
+    costs torch's fp32 gelu up to 5e-7 absolute there."""
+    import math
+
+    ins = O.make_inputs("fused_gelu", (10007,), "float32", 0)
+    ref = O.reference("fused_gelu", ins)
+    x, b = ins[0].double().tolist(), ins[1].double().tolist()
+    w = float(torch.tensor(O.FUSED_SCALE, dtype=torch.float32))
+    want = []
+    for xi, bi in zip(x, b):
+        z = float(np.float32(np.float32(xi) * np.float32(w)) + np.float32(bi))
+        want.append(0.5 * z * (1.0 + math.erf(z / math.sqrt(2.0))))
+    want = torch.tensor(want, dtype=torch.float64)
+    err = (ref.double() - want).abs()
+    assert (err <= 4 * 2.0 ** -23 * want.abs() + 1e-6).all(), float(err.max())
