@@ -562,6 +562,7 @@ struct AttnDualShared {
 };
 
 constexpr int kAttnDualThreads = 384;
+constexpr int kAttnCausalGroup = 16;  // heads per longest-first group (causal grids)
 // Register split: the kernel launches at 65536 / 384 = 168 registers per
 // thread (64512 for the CTA); the warpgroup of producers, MMA issuer and
 // TMEM owner gives back down to kAttnDualLowRegs and each softmax
@@ -866,8 +867,8 @@ template <typename T, int FMT, int BN, int D, bool CAUSAL>
 __global__ void __launch_bounds__(kAttnDualThreads, 1)
     attn_tc_dual_kernel(const __grid_constant__ CUtensorMap tma_q,
                         const __grid_constant__ CUtensorMap tma_k,
-                        const __grid_constant__ CUtensorMap tma_v, T* __restrict__ O, int S,
-                        int stages, float scale_log2, unsigned int* err) {
+                        const __grid_constant__ CUtensorMap tma_v, T* __restrict__ O, int BH,
+                        int S, int stages, float scale_log2, unsigned int* err) {
   using G = AttnDualGeom<D>;
   constexpr uint32_t KV_SLOT = ((static_cast<uint32_t>(BN) * D * G::ES) + 1023u) & ~1023u;
   constexpr int COLS = 2 * D + 2 * BN;
@@ -884,11 +885,25 @@ __global__ void __launch_bounds__(kAttnDualThreads, 1)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int spans = (S + 255) / 256;
-  // longest causal spans first; identity order for the non-causal task
-  const int span = CAUSAL ? (spans - 1 - static_cast<int>(blockIdx.x))
-                          : static_cast<int>(blockIdx.x);
+  int span, bh;
+  if constexpr (CAUSAL) {
+    // Longest spans first across groups of kAttnCausalGroup heads (one
+    // 1-D grid): the block scheduler then hands out work longest first
+    // over the whole GPU (a per-head order leaves short spans of the
+    // first heads and long spans of the last ones in the same wave), while
+    // the K/V of the heads in flight stay within L2.
+    const int i = static_cast<int>(blockIdx.x);
+    const int per_group = kAttnCausalGroup * spans;
+    const int g = i / per_group;
+    const int r = i - g * per_group;
+    const int gh = min(kAttnCausalGroup, BH - g * kAttnCausalGroup);
+    span = spans - 1 - r / gh;
+    bh = g * kAttnCausalGroup + r % gh;
+  } else {
+    span = static_cast<int>(blockIdx.x);
+    bh = static_cast<int>(blockIdx.y);
+  }
   const int q0 = span * 256;  // tile t: query rows [q0 + 128 t, +128)
-  const int bh = blockIdx.y;
   auto blocks_of = [&](int t) {
     const int len = CAUSAL ? min(S, q0 + 128 * (t + 1)) : S;
     return (len + BN - 1) / BN;
@@ -1025,8 +1040,9 @@ static gpo_status plan_attention_dual(const gpo_key& k, Plan& p, std::string& lo
   p.res.smem_bytes = smem;
   p.res.tmem_cols = static_cast<uint32_t>(attn_tmem_alloc(cols));
   p.res.threads_per_cta = static_cast<uint32_t>(kAttnDualThreads);
-  p.res.grid_x = static_cast<uint32_t>(cdiv(k.shape[1], 256));
-  p.res.grid_y = static_cast<uint32_t>(k.shape[0]);
+  const bool causal = k.task == GPO_TASK_ATTENTION_CAUSAL;
+  p.res.grid_x = static_cast<uint32_t>(cdiv(k.shape[1], 256) * (causal ? k.shape[0] : 1));
+  p.res.grid_y = static_cast<uint32_t>(causal ? 1 : k.shape[0]);
   p.res.grid_z = 1;
   p.res.launches_per_call = 1;
   snprintf(p.res.kernel, sizeof(p.res.kernel), "attn_tc_dual_kernel<%s,BN=%d,D=%d,%s,two_tiles>",
@@ -1144,11 +1160,12 @@ static gpo_status run_attn_tc_dual(const gpo_key& k, const Plan& p, const gpo_ar
   const uint32_t dyn = static_cast<uint32_t>(p.aux[0]);
   gpo_status s = ensure_smem_attr(reinterpret_cast<const void*>(kern), dyn);
   if (s != GPO_OK) return s;
-  const dim3 grid(static_cast<unsigned>(cdiv(S, 256)), static_cast<unsigned>(BH));
+  const dim3 grid = CAUSAL ? dim3(static_cast<unsigned>(cdiv(S, 256) * BH), 1)
+                           : dim3(static_cast<unsigned>(cdiv(S, 256)), static_cast<unsigned>(BH));
   const float scale_log2 = 1.4426950408889634f / sqrtf(static_cast<float>(D));
   kern<<<grid, kAttnDualThreads, dyn, c.stream>>>(mq, mk, mv, static_cast<T*>(a.out),
-                                                  static_cast<int>(S), k.num_stages, scale_log2,
-                                                  c.err);
+                                                  static_cast<int>(BH), static_cast<int>(S),
+                                                  k.num_stages, scale_log2, c.err);
   return launch_status();
 }
 

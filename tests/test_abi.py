@@ -106,7 +106,11 @@ def test_attention_plans():
     rd = compile_module("attention_causal", (128, 4096, 128),
                         {**base, "BLOCK_M": 256, "num_warps": 8}).resources()
     assert rd["kernel"] == "attn_tc_dual_kernel<bf16,BN=128,D=128,causal,two_tiles>"
-    assert rd["grid"] == [16, 128, 1] and rd["threads_per_cta"] == 384
+    # causal: one 1-D grid ordered longest span first over groups of heads
+    assert rd["grid"] == [16 * 128, 1, 1] and rd["threads_per_cta"] == 384
+    rf = compile_module("attention", (128, 4096, 128),
+                        {**base, "BLOCK_M": 256, "num_warps": 8}).resources()
+    assert rf["grid"] == [16, 128, 1]
     assert rd["tmem_cols"] == 512 and rd["smem_bytes"] <= 227 * 1024
     for bad in ({"num_stages": 3}, {"BLOCK_N": 128, "num_stages": 4}):  # shared memory
         with pytest.raises(KernelBuildError, match="shared memory"):
