@@ -670,10 +670,14 @@ __device__ __forceinline__ void attn_dual_mma(AttnDualShared& sh, uint32_t tmem,
     const uint32_t vs = v_smem + static_cast<uint32_t>(j % stages) * KV_SLOT;
     const uint32_t pa = tmem + static_cast<uint32_t>(2 * D + t * BN);
     const uint32_t o_tmem = tmem + static_cast<uint32_t>(t * D);
-    // keys [0, BN/2) as soon as their P is stored, then the rest
+    // keys [0, BN/2) as soon as their P is stored, then the rest; when the
+    // second half is already released (every softmax warp releases the
+    // first half before the second), one test replaces both waits
+    const uint32_t par = static_cast<uint32_t>(j) & 1u;
+    const bool all_ready = mbar_test_wait(smem_u32(&sh.p_full[t][1]), par);
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
-      if (!wait(&sh.p_full[t][h], static_cast<uint32_t>(j) & 1u)) return false;
+      if (!all_ready && !wait(&sh.p_full[t][h], par)) return false;
       tc_fence_after();
 #pragma unroll
       for (int kk = h * (BN / 32); kk < (h + 1) * (BN / 32); ++kk) {
