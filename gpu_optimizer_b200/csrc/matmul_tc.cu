@@ -73,6 +73,34 @@ __device__ __forceinline__ void tile_coords(int tile, int num_pid_m, int num_pid
   pn = (tile % in_group) / gsize;
 }
 
+// Work items of a persistent CTA-pair matmul over G clusters.  The tiles
+// fill W = T / G whole waves; when the R = T - W*G tiles of the last wave
+// leave more than half of the clusters idle (2R <= G), each of them is
+// split into two column halves, so the last wave takes the time of half a
+// tile instead of a whole one.  Item i < W*G (or every item without a
+// split) is tile i; the rest are (tile, half) pairs.
+struct Tc2Items {
+  int full;   // items that are whole tiles
+  int count;  // all items
+  __device__ __forceinline__ void at(int item, int& tile, int& half) const {
+    if (item < full) {
+      tile = item;
+      half = -1;
+    } else {
+      tile = full + (item - full) / 2;
+      half = (item - full) & 1;
+    }
+  }
+};
+
+__device__ __forceinline__ Tc2Items tc2_items(int num_tiles, int clusters, bool can_split) {
+  const int waves = num_tiles / clusters;
+  const int rest = num_tiles - waves * clusters;
+  if (can_split && rest > 0 && 2 * rest <= clusters)
+    return {waves * clusters, waves * clusters + 2 * rest};
+  return {num_tiles, num_tiles};
+}
+
 // Issue the MMAs of one K block: KS steps of 32 bytes of K (KS =
 // BLOCK_K * es / 32, so the A swizzle width min(KS * 32, 128) is known at
 // compile time too).  a0 / b0 are the descriptors of this ring slot at K
@@ -377,6 +405,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PERSISTENT ? 256 : 1
   constexpr int ALLOC = tc2_tmem_alloc(ACC * BN);
   constexpr int KSTEP = 32 / ES;
   constexpr uint32_t IDESC = make_idesc(FMT, 256, BN, false, true);
+  // A half tile (last wave of a persistent grid) covers BN/2 columns: each
+  // CTA stages one B chunk instead of two and the MMAs run with N = BN/2.
+  constexpr bool CAN_SPLIT = PERSISTENT && FMT != 2 && (BNH * ES) / SWB == 2;
+  constexpr uint32_t IDESC_HALF = make_idesc(FMT, 256, BN / 2, false, true);
 
   __shared__ TcShared sh;
   extern __shared__ uint8_t dyn_smem[];
@@ -392,6 +424,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PERSISTENT ? 256 : 1
   const int num_tiles = num_pid_m * num_pid_n;
   const int first_tile = static_cast<int>(blockIdx.x >> 1);
   const int tile_step = PERSISTENT ? static_cast<int>(gridDim.x >> 1) : num_tiles;
+  const Tc2Items items = tc2_items(num_tiles, tile_step, CAN_SPLIT);
   const int num_kb = (K + BK - 1) / BK;
 
   if (threadIdx.x == 0) {
@@ -425,26 +458,30 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PERSISTENT ? 256 : 1
     int it = 0, s = 0;  // K blocks issued; ring slot and phase of the next one
     uint32_t ph = 0;
     bool ok = true;
-    for (int tile = first_tile; tile < num_tiles && ok; tile += tile_step) {
-      int pm, pn;
+    for (int item = first_tile; item < items.count && ok; item += tile_step) {
+      int tile, half, pm, pn;
+      items.at(item, tile, half);
       tile_coords(tile, num_pid_m, num_pid_n, group_m, pm, pn);
+      // B columns this CTA stages: [n0, n0 + chunks * SWB / ES)
+      const int chunks = half < 0 ? (BNH * ES) / SWB : 1;
+      const int n0 = half < 0 ? pn * BN + static_cast<int>(rank) * BNH
+                              : pn * BN + half * BNH + static_cast<int>(rank) * (BNH / 2);
+      const uint32_t stage_tx = 2u * (a_bytes + (half < 0 ? b_bytes : b_bytes / 2));
       for (int kb = 0; kb < num_kb; ++kb, ++it) {
         if (!mbar_wait(smem_u32(&sh.empty[s]), ph ^ 1u, abort_flag, err, kErrWaitProducer)) {
           ok = false;
           break;
         }
         const uint32_t full = full0 + static_cast<uint32_t>(s) * 8u;
-        if (rank == 0) mbar_arrive_expect_tx(smem_u32(&sh.full[s]), 2u * (a_bytes + b_bytes));
+        if (rank == 0) mbar_arrive_expect_tx(smem_u32(&sh.full[s]), stage_tx);
         const uint32_t sa = smem_base + s * stage_bytes;
         const uint32_t sb = sa + a_bytes;
         const int a_atoms = (BK * ES) / swa;
         for (int a = 0; a < a_atoms; ++a)
           tma_load_2d_pair(sa + a * 128 * swa, &tma_a, full, kb * BK + a * (swa / ES),
                            pm * 256 + static_cast<int>(rank) * 128);
-#pragma unroll
-        for (int c = 0; c < (BNH * ES) / SWB; ++c)
-          tma_load_2d_pair(sb + c * BK * SWB, &tma_b, full,
-                           pn * BN + static_cast<int>(rank) * BNH + c * (SWB / ES), kb * BK);
+        for (int c = 0; c < chunks; ++c)
+          tma_load_2d_pair(sb + c * BK * SWB, &tma_b, full, n0 + c * (SWB / ES), kb * BK);
         if (++s == stages) {
           s = 0;
           ph ^= 1u;
@@ -477,7 +514,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PERSISTENT ? 256 : 1
         FMT == 2 ? (make_smem_desc(smem_base + a_bytes, BK * SWB, 4 * SWB, 0) | (1ull << 61))
                  : make_smem_desc(smem_base + a_bytes, BK * SWB, 8 * SWB, SWB);
     const int ksteps = BK / KSTEP;
-    for (int tile = first_tile; tile < num_tiles && ok; tile += tile_step, ++tcount) {
+    for (int item = first_tile; item < items.count && ok; item += tile_step, ++tcount) {
+      int tile, half;
+      items.at(item, tile, half);
+      const uint32_t idesc = half < 0 ? IDESC : IDESC_HALF;
       const int buf = tcount % ACC;
       const uint32_t use = static_cast<uint32_t>(tcount / ACC);
       if (PERSISTENT && !mbar_wait<true>(smem_u32(&sh.acc_empty[buf]), (use & 1u) ^ 1u,
@@ -495,7 +535,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PERSISTENT ? 256 : 1
         tc_fence_after();
         const uint32_t so4 = (static_cast<uint32_t>(s) * stage_bytes) >> 4;
         issue_kblock_any<ES, 128, SWB, 1, BN, FMT, true>(ksteps, d_tmem, adesc0 + so4,
-                                                         bdesc0 + so4, IDESC, kb == 0);
+                                                         bdesc0 + so4, idesc, kb == 0);
         mma_commit_pair(smem_u32(&sh.empty[s]));
         mma_commit_pair(peer_empty0 + static_cast<uint32_t>(s) * 8u);
         if (++s == stages) {
@@ -520,24 +560,29 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PERSISTENT ? 256 : 1
     const int q = warp & 3;
     const uint32_t leader_acc_empty0 = mapa_shared(smem_u32(&sh.acc_empty[0]), 0);
     int tcount = 0;
-    for (int tile = first_tile; tile < num_tiles; tile += tile_step, ++tcount) {
+    for (int item = first_tile; item < items.count; item += tile_step, ++tcount) {
       const int buf = tcount % ACC;
       const uint32_t use = static_cast<uint32_t>(tcount / ACC);
       if (!mbar_wait_idle(smem_u32(&sh.acc_full[buf]), use & 1u, abort_flag, err,
                           kErrWaitEpilogue))
         break;
       tc_fence_after();
-      int pm, pn;
+      int tile, half, pm, pn;
+      items.at(item, tile, half);
       tile_coords(tile, num_pid_m, num_pid_n, group_m, pm, pn);
       const int row = pm * 256 + static_cast<int>(rank) * 128 + q * 32 + lane;
+      // a half tile's accumulator holds its BN/2 columns in the first BN/2
+      // TMEM columns of the buffer
+      const int ncols = half < 0 ? BN : BN / 2;
+      const int cbase = pn * BN + (half < 0 ? 0 : half * (BN / 2));
 #pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
+      for (int c = 0; c < ncols / 32; ++c) {
         uint32_t r[32];
         tmem_ld32(tmem_base + (static_cast<uint32_t>(q * 32) << 16) +
                       static_cast<uint32_t>(buf * BN + c * 32),
                   r);
         tmem_wait_ld();
-        const int col0 = pn * BN + c * 32;
+        const int col0 = cbase + c * 32;
         if (row < M) {
           T* dst = C + static_cast<int64_t>(row) * N + col0;
           if (col0 + 32 <= N) {
