@@ -176,13 +176,16 @@ def run_ours(args, rank, world, local):
     for kc in kcs:
         warm_compile(kc)
     stream = torch.cuda.current_stream()
+    # the clock sampler starts first; the warm-up steps then run right
+    # before the timed ones, so the timed region does not begin on a GPU
+    # that idled (and lowered its clock) while the sampler started
+    clocks = ClockSampler(local)
+    time.sleep(0.3)
+    barrier(world)
     for i in range(args.warmup):
         kcs[i % N_SETS].fn()
     torch.cuda.synchronize()
     check_device_status()
-
-    clocks = ClockSampler(local)
-    time.sleep(0.3)
     barrier(world)
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
