@@ -647,27 +647,38 @@ __device__ __forceinline__ void attn_dual_mma(AttnDualShared& sh, uint32_t tmem,
   constexpr uint32_t KV_SLOT = ((static_cast<uint32_t>(BN) * D * G::ES) + 1023u) & ~1023u;
   constexpr uint32_t IDESC_S = make_idesc(FMT, 128, BN, false, false);
   constexpr uint32_t IDESC_O = make_idesc(FMT, 128, D, false, true);
+  // The tensor pipe runs these MMAs back to back only while this thread
+  // issues them faster than they execute, so the work between two groups
+  // is kept short: descriptors are built once and advanced by constant
+  // offsets (a descriptor's address field is the byte address >> 4, and
+  // every shared-memory address stays below 256 KB), ring positions are
+  // stepped without division, and each wait first tests the phase without
+  // blocking, since the awaited phase has usually completed by then.
   auto wait = [&](const uint64_t* bar, uint32_t parity) {
-    return mbar_wait(smem_u32(bar), parity, abort_flag, err, kErrWaitMma);
+    const uint32_t b = smem_u32(bar);
+    return mbar_test_wait(b, parity) || mbar_wait(b, parity, abort_flag, err, kErrWaitMma);
   };
-  bool ok = wait(&sh.q_full, 0);
-  auto s_mma = [&](int t, int j) {
-    const uint32_t ks = k_smem + static_cast<uint32_t>(j % stages) * KV_SLOT;
-    const uint32_t qs = q_smem + static_cast<uint32_t>(t) * G::Q_BYTES;
+  constexpr uint64_t HI = smem_desc_hi(8 * SW, SW);  // Q, K (K-major) and V (MN-major)
+  const uint32_t q_lo = smem_desc_lo(q_smem, 16);
+  const uint32_t k_lo = smem_desc_lo(k_smem, 16);
+  const uint32_t v_lo = smem_desc_lo(v_smem, BN * SW);
+  auto s_mma = [&](int t, int k_slot) {
+    const uint32_t qd = q_lo + static_cast<uint32_t>(t) * (G::Q_BYTES >> 4);
+    const uint32_t kd = k_lo + static_cast<uint32_t>(k_slot) * (KV_SLOT >> 4);
     const uint32_t s_tmem = tmem + static_cast<uint32_t>(2 * D + t * BN);
 #pragma unroll
     for (int kk = 0; kk < D / 16; ++kk) {
       const uint32_t kbyte = static_cast<uint32_t>(kk) * 32u;
       const uint32_t aoff = (kbyte / SW) * (128 * SW) + (kbyte % SW);
       const uint32_t boff = (kbyte / SW) * (BN * SW) + (kbyte % SW);
-      mma_f16_ss(s_tmem, make_smem_desc(qs + aoff, 16, 8 * SW, SW),
-                 make_smem_desc(ks + boff, 16, 8 * SW, SW), IDESC_S, kk > 0 ? 1u : 0u);
+      mma_f16_ss(s_tmem, HI | (qd + (aoff >> 4)), HI | (kd + (boff >> 4)), IDESC_S,
+                 kk > 0 ? 1u : 0u);
     }
     mma_commit(smem_u32(&sh.s_full[t]));
   };
   // P_t sits in the first BN/2 columns of tile t's S/P buffer
-  auto pv_mma = [&](int t, int j, bool last) {
-    const uint32_t vs = v_smem + static_cast<uint32_t>(j % stages) * KV_SLOT;
+  auto pv_mma = [&](int t, int v_slot, int j, bool last) {
+    const uint32_t vd = v_lo + static_cast<uint32_t>(v_slot) * (KV_SLOT >> 4);
     const uint32_t pa = tmem + static_cast<uint32_t>(2 * D + t * BN);
     const uint32_t o_tmem = tmem + static_cast<uint32_t>(t * D);
     // keys [0, BN/2) as soon as their P is stored, then the rest; when the
@@ -675,29 +686,41 @@ __device__ __forceinline__ void attn_dual_mma(AttnDualShared& sh, uint32_t tmem,
     // first half before the second), one test replaces both waits
     const uint32_t par = static_cast<uint32_t>(j) & 1u;
     const bool all_ready = mbar_test_wait(smem_u32(&sh.p_full[t][1]), par);
+    if (all_ready) tc_fence_after();
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
-      if (!all_ready && !wait(&sh.p_full[t][h], par)) return false;
-      tc_fence_after();
-#pragma unroll
-      for (int kk = h * (BN / 32); kk < (h + 1) * (BN / 32); ++kk) {
-        const uint64_t bdesc = make_smem_desc(vs + kk * 16 * SW, BN * SW, 8 * SW, SW);
-        mma_f16_ts(o_tmem, pa + static_cast<uint32_t>(kk * 8), bdesc, IDESC_O,
-                   (j > 0 || kk > 0) ? 1u : 0u);
+      if (!all_ready) {
+        if (!wait(&sh.p_full[t][h], par)) return false;
+        tc_fence_after();
       }
+#pragma unroll
+      for (int kk = h * (BN / 32); kk < (h + 1) * (BN / 32); ++kk)
+        mma_f16_ts(o_tmem, pa + static_cast<uint32_t>(kk * 8),
+                   HI | (vd + static_cast<uint32_t>((kk * 16 * SW) >> 4)), IDESC_O,
+                   (j > 0 || kk > 0) ? 1u : 0u);
     }
     if (last) mma_commit(smem_u32(&sh.pv_done[t]));  // for the epilogue
     return true;
   };
+  bool ok = wait(&sh.q_full, 0);
   if (ok) ok = wait(&sh.k_full[0], 0);
   if (ok) {
     tc_fence_after();
     s_mma(0, 0);
     s_mma(1, 0);
   }
+  // ring positions: V of block j, K of block j + 1
+  int v_slot = 0, k_slot = 0;
+  uint32_t v_par = 0, k_par = 0;
+  auto step = [&](int& slot, uint32_t& parity) {
+    if (++slot == stages) {
+      slot = 0;
+      parity ^= 1u;
+    }
+  };
+  step(k_slot, k_par);
   for (int j = 0; j < nb1 && ok; ++j) {
-    const int sv = j % stages;
-    if (!wait(&sh.v_full[sv], static_cast<uint32_t>(j / stages) & 1u)) {
+    if (!wait(&sh.v_full[v_slot], v_par)) {
       ok = false;
       break;
     }
@@ -705,17 +728,18 @@ __device__ __forceinline__ void attn_dual_mma(AttnDualShared& sh, uint32_t tmem,
 #pragma unroll
     for (int t = 0; t < 2; ++t) {
       const int nbt = t == 0 ? nb0 : nb1;
-      if (ok && j < nbt) ok = pv_mma(t, j, j + 1 == nbt);
+      if (ok && j < nbt) ok = pv_mma(t, v_slot, j, j + 1 == nbt);
       if (ok && j + 1 < nbt) {
         if (!k_ready) {
-          const int sk = (j + 1) % stages;
-          ok = wait(&sh.k_full[sk], static_cast<uint32_t>((j + 1) / stages) & 1u);
+          ok = wait(&sh.k_full[k_slot], k_par);
           tc_fence_after();
           k_ready = true;
         }
-        if (ok) s_mma(t, j + 1);
+        if (ok) s_mma(t, k_slot);
       }
     }
+    step(v_slot, v_par);
+    step(k_slot, k_par);
   }
   if (!ok) {
     mma_commit(smem_u32(&sh.drain));

@@ -383,6 +383,19 @@ __device__ __forceinline__ uint64_t make_smem_desc(uint32_t saddr, uint32_t lbo_
   return d;
 }
 
+// The same descriptor in two halves: the upper 32 bits (stride byte
+// offset, version, swizzle) are a compile-time constant of the operand
+// layout, the lower 32 bits hold the start address and the leading byte
+// offset.  desc = hi | lo; lo + (bytes >> 4) moves the start address while
+// the address stays below 256 KB.
+__host__ __device__ constexpr uint64_t smem_desc_hi(uint32_t sbo_bytes, int swizzle_bytes) {
+  return (static_cast<uint64_t>((sbo_bytes >> 4) & 0x3FFFu) << 32) | (1ull << 46) |
+         (static_cast<uint64_t>(swizzle_code(swizzle_bytes)) << 61);
+}
+__device__ __forceinline__ uint32_t smem_desc_lo(uint32_t saddr, uint32_t lbo_bytes) {
+  return ((saddr >> 4) & 0x3FFFu) | (((lbo_bytes >> 4) & 0x3FFFu) << 16);
+}
+
 // Instruction descriptor for kind::f16 / kind::tf32 with fp32 accumulation.
 // fmt: 0 = f16, 1 = bf16, 2 = tf32.  a_mn / b_mn: operand is MN-major.
 __host__ __device__ constexpr uint32_t make_idesc(int fmt, int M, int N, bool a_mn, bool b_mn) {
