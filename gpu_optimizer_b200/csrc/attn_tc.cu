@@ -731,8 +731,9 @@ __device__ __forceinline__ void attn_dual_mma(AttnDualShared& sh, uint32_t tmem,
       if (ok && j < nbt) ok = pv_mma(t, v_slot, j, j + 1 == nbt);
       if (ok && j + 1 < nbt) {
         if (!k_ready) {
+          // K arrives by TMA (async proxy, like the MMA's reads): the
+          // barrier's phase alone orders it, no tcgen05 fence
           ok = wait(&sh.k_full[k_slot], k_par);
-          tc_fence_after();
           k_ready = true;
         }
         if (ok) s_mma(t, k_slot);
