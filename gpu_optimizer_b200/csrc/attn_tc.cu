@@ -41,6 +41,7 @@
 // fit in 256 and shared memory holds two CTAs, NB = 2 and two CTAs share
 // each SM.
 #include <algorithm>
+#include <atomic>
 
 #include "gpo_common.cuh"
 #include "gpo_internal.h"
@@ -556,6 +557,11 @@ struct AttnDualShared {
   uint64_t s_full[2];
   uint64_t p_full[2][2];  // [tile][half of the block's keys]
   uint64_t pv_done[2];
+  uint64_t q_empty;    // the item's last S MMAs are done: Q may be reloaded
+  uint64_t o_free[2];  // the epilogue has read O_t out of TMEM
+  uint64_t item_full[2];   // the CTA's next work item is published in item[]
+  uint64_t item_empty[2];  // every other role has read it: the slot is free
+  int item[2];             // work item of the CTA's it-th turn at [it & 1]; -1: none
   uint64_t drain;
   uint32_t tmem_base;
   int abort;
@@ -567,12 +573,82 @@ constexpr int kAttnCausalGroup = 16;  // heads per longest-first group (causal g
 // thread (64512 for the CTA); the warpgroup of producers, MMA issuer and
 // TMEM owner gives back down to kAttnDualLowRegs and each softmax
 // warpgroup (a 128-column S row per thread) grows to kAttnDualHighRegs:
-// 128 * 56 + 256 * 224 = 64512, the launch's total, so every increase
-// is covered.
-constexpr int kAttnDualLowRegs = 56;
-constexpr int kAttnDualHighRegs = 224;
+// 128 * 88 + 256 * 208 = 64512, the launch's total, so every increase
+// is covered (the persistent MMA thread spills below 88).
+constexpr int kAttnDualLowRegs = 88;
+constexpr int kAttnDualHighRegs = 208;
 static_assert(128 * kAttnDualLowRegs + 256 * kAttnDualHighRegs <= 168 * kAttnDualThreads,
               "register split exceeds the launch's registers");
+
+// Work items of the persistent two-tile kernel are handed out in order by
+// an atomic counter: a CTA takes the next item when it starts one, so the
+// causal spans of different lengths spread evenly over the SMs (a fixed
+// round-robin of the same order left the busiest SM 10 % above the mean).
+// Each launch uses one of kAttnWorkSlots counter pairs {next item, CTAs
+// done}, chosen round-robin by the host; the last CTA to finish sets its
+// pair back to zero for the next launch that gets the slot.  Launches that
+// overlap on one device use different slots unless more than
+// kAttnWorkSlots of them run at once.
+constexpr int kAttnWorkSlots = 64;
+__device__ unsigned int g_attn_work[kAttnWorkSlots][2];
+
+// Work item i: the 256-row query span and head it covers.  Full attention walks the
+// spans of one head after another, so the CTAs in flight share the K/V of
+// a few heads in L2.  Causal spans go longest first across groups of
+// kAttnCausalGroup heads: items are then handed out longest first over the
+// whole GPU (a per-head order leaves short spans of the first heads and
+// long spans of the last ones in the same wave), while the K/V of the heads
+// in flight stay within L2.
+template <bool CAUSAL>
+__device__ __forceinline__ void attn_dual_item(int i, int spans, int BH, int& span, int& bh) {
+  if constexpr (CAUSAL) {
+    const int per_group = kAttnCausalGroup * spans;
+    const int g = i / per_group;
+    const int r = i - g * per_group;
+    const int gh = min(kAttnCausalGroup, BH - g * kAttnCausalGroup);
+    span = spans - 1 - r / gh;
+    bh = g * kAttnCausalGroup + r % gh;
+  } else {
+    span = i % spans;
+    bh = i / spans;
+  }
+}
+
+// K/V blocks of query tile t (0 or 1) of the span starting at row q0.
+template <int BN, bool CAUSAL>
+__device__ __forceinline__ int attn_dual_blocks(int S, int q0, int t) {
+  const int len = CAUSAL ? min(S, q0 + 128 * (t + 1)) : S;
+  return (len + BN - 1) / BN;
+}
+
+// The item of the CTA's it-th turn, published by the K producer (-1: no
+// more work); the caller's warp (all lanes, WARP) or thread has read it once
+// it returns.  Returns false when the wait fails.
+constexpr int kAttnItemReaders = 10;  // V producer, MMA thread, 8 softmax warps
+template <bool WARP>
+__device__ __forceinline__ bool attn_dual_next_item(AttnDualShared& sh, int it,
+                                                    volatile int* abort_flag, unsigned int* err,
+                                                    uint32_t site, int& item) {
+  if (!mbar_wait(smem_u32(&sh.item_full[it & 1]), static_cast<uint32_t>(it >> 1) & 1u,
+                 abort_flag, err, site))
+    return false;
+  item = *reinterpret_cast<volatile int*>(&sh.item[it & 1]);
+  if (WARP) __syncwarp();
+  if (!WARP || (threadIdx.x & 31) == 0) mbar_arrive(smem_u32(&sh.item_empty[it & 1]));
+  return true;
+}
+
+// Position in a ring of `stages` slots: slot and the parity of its round.
+struct RingPos {
+  int slot = 0;
+  uint32_t parity = 0;
+  __device__ __forceinline__ void step(int stages) {
+    if (++slot == stages) {
+      slot = 0;
+      parity ^= 1u;
+    }
+  }
+};
 
 template <int N>
 __device__ __forceinline__ void regs_dec() {
@@ -590,56 +666,96 @@ struct AttnDualGeom {
   static constexpr uint32_t Q_BYTES = 128u * D * ES;           // one query tile
 };
 
-// TMA producer of Q (both tiles) and the K ring (is_k), or of the V ring.
-template <int BN, int D>
+// TMA producer of Q (both tiles of each item) and the K ring (is_k), or of
+// the V ring.  The rings run on across items: every item loads the nb1
+// blocks of its tile 1.
+template <int BN, int D, bool CAUSAL>
 __device__ __forceinline__ void attn_dual_producer(const CUtensorMap* tma_q,
                                                    const CUtensorMap* map, AttnDualShared& sh,
-                                                   uint32_t q_smem, uint32_t ring, int q0, int bh,
-                                                   int nblk, int stages, bool is_k,
+                                                   uint32_t q_smem, uint32_t ring, int S,
+                                                   int BH, int stages, int work_slot, bool is_k,
                                                    volatile int* abort_flag, unsigned int* err) {
   using G = AttnDualGeom<D>;
   constexpr uint32_t KV_BYTES = static_cast<uint32_t>(BN) * D * G::ES;
   constexpr uint32_t KV_SLOT = (KV_BYTES + 1023u) & ~1023u;
   uint64_t* full = is_k ? sh.k_full : sh.v_full;
   uint64_t* empty = is_k ? sh.k_empty : sh.v_empty;
+  const int spans = (S + 255) / 256;
+  const int items = spans * BH;
   bool ok = true;
-  int issued = 0;
-  if (is_k) {
-    mbar_arrive_expect_tx(smem_u32(&sh.q_full), 2u * G::Q_BYTES);
+  int issued = 0;      // ring loads issued (over all items)
+  int q_loads = 0;     // Q loads issued
+  RingPos pos;
+  for (int it = 0; ok; ++it) {
+    int item;
+    if (is_k) {
+      // take the next item and publish it to the CTA's other roles, once
+      // they have all read the item published two turns ago in this slot
+      if (it >= 2 && !mbar_wait(smem_u32(&sh.item_empty[it & 1]),
+                                static_cast<uint32_t>((it >> 1) - 1) & 1u, abort_flag, err,
+                                kErrWaitProducer)) {
+        ok = false;
+        break;
+      }
+      const int next = static_cast<int>(atomicAdd(&g_attn_work[work_slot][0], 1u));
+      item = next < items ? next : -1;
+      sh.item[it & 1] = item;
+      mbar_arrive(smem_u32(&sh.item_full[it & 1]));
+    } else {
+      ok = attn_dual_next_item<false>(sh, it, abort_flag, err, kErrWaitProducer, item);
+    }
+    if (!ok || item < 0) break;
+    int span, bh;
+    attn_dual_item<CAUSAL>(item, spans, BH, span, bh);
+    const int q0 = span * 256;
+    const int nblk = attn_dual_blocks<BN, CAUSAL>(S, q0, 1);
+    if (is_k) {
+      // Q of the previous item is free once its last S MMAs are done
+      if (it > 0 && !mbar_wait(smem_u32(&sh.q_empty), static_cast<uint32_t>(it - 1) & 1u,
+                               abort_flag, err, kErrWaitProducer)) {
+        ok = false;
+        break;
+      }
+      mbar_arrive_expect_tx(smem_u32(&sh.q_full), 2u * G::Q_BYTES);
 #pragma unroll
-    for (int t = 0; t < 2; ++t)
+      for (int t = 0; t < 2; ++t)
+#pragma unroll
+        for (int a = 0; a < (D * G::ES) / G::SW; ++a)
+          tma_load_3d(q_smem + t * G::Q_BYTES + a * 128 * G::SW, tma_q, smem_u32(&sh.q_full),
+                      a * (G::SW / G::ES), q0 + 128 * t, bh);
+      ++q_loads;
+    }
+    for (int j = 0; j < nblk; ++j) {
+      if (!mbar_wait(smem_u32(&empty[pos.slot]), pos.parity ^ 1u, abort_flag, err,
+                     kErrWaitProducer)) {
+        ok = false;
+        break;
+      }
+      const uint32_t dst = ring + static_cast<uint32_t>(pos.slot) * KV_SLOT;
+      mbar_arrive_expect_tx(smem_u32(&full[pos.slot]), KV_BYTES);
+      // K: rows [j*BN, +BN) in K-major atoms; V: the same rows, MN-major
+      // column chunks (the B operand of the PV MMA)
 #pragma unroll
       for (int a = 0; a < (D * G::ES) / G::SW; ++a)
-        tma_load_3d(q_smem + t * G::Q_BYTES + a * 128 * G::SW, tma_q, smem_u32(&sh.q_full),
-                    a * (G::SW / G::ES), q0 + 128 * t, bh);
-  }
-  for (int j = 0; j < nblk; ++j) {
-    const int s = j % stages;
-    const uint32_t r = static_cast<uint32_t>(j / stages);
-    if (!mbar_wait(smem_u32(&empty[s]), (r & 1u) ^ 1u, abort_flag, err, kErrWaitProducer)) {
-      ok = false;
-      break;
+        tma_load_3d(dst + a * BN * G::SW, map, smem_u32(&full[pos.slot]), a * (G::SW / G::ES),
+                    j * BN, bh);
+      ++issued;
+      pos.step(stages);
     }
-    const uint32_t dst = ring + static_cast<uint32_t>(s) * KV_SLOT;
-    mbar_arrive_expect_tx(smem_u32(&full[s]), KV_BYTES);
-    // K: rows [j*BN, +BN) in K-major atoms; V: the same rows, MN-major
-    // column chunks (the B operand of the PV MMA)
-#pragma unroll
-    for (int a = 0; a < (D * G::ES) / G::SW; ++a)
-      tma_load_3d(dst + a * BN * G::SW, map, smem_u32(&full[s]), a * (G::SW / G::ES), j * BN, bh);
-    issued = j + 1;
   }
   if (!ok) {
-    if (is_k) mbar_wait_drain(smem_u32(&sh.q_full), 0, err);
-    for (int j = max(0, issued - stages); j < issued; ++j)
-      mbar_wait_drain(smem_u32(&full[j % stages]), static_cast<uint32_t>(j / stages) & 1u, err);
+    // let the copies in flight land before the CTA can exit
+    if (q_loads > 0)
+      mbar_wait_drain(smem_u32(&sh.q_full), static_cast<uint32_t>(q_loads - 1) & 1u, err);
+    for (int g = max(0, issued - stages); g < issued; ++g)
+      mbar_wait_drain(smem_u32(&full[g % stages]), static_cast<uint32_t>(g / stages) & 1u, err);
   }
 }
 
 // MMA issuer: S_t(j) = Q_t K_j^T and O_t += P_t(j) V_j, tiles alternating.
-template <int FMT, int BN, int D>
+template <int FMT, int BN, int D, bool CAUSAL>
 __device__ __forceinline__ void attn_dual_mma(AttnDualShared& sh, uint32_t tmem, uint32_t q_smem,
-                                              uint32_t k_smem, uint32_t v_smem, int nb0, int nb1,
+                                              uint32_t k_smem, uint32_t v_smem, int S, int BH,
                                               int stages, volatile int* abort_flag,
                                               unsigned int* err) {
   using G = AttnDualGeom<D>;
@@ -677,14 +793,13 @@ __device__ __forceinline__ void attn_dual_mma(AttnDualShared& sh, uint32_t tmem,
     mma_commit(smem_u32(&sh.s_full[t]));
   };
   // P_t sits in the first BN/2 columns of tile t's S/P buffer
-  auto pv_mma = [&](int t, int v_slot, int j, bool last) {
+  auto pv_mma = [&](int t, int v_slot, int j, uint32_t par, bool last) {
     const uint32_t vd = v_lo + static_cast<uint32_t>(v_slot) * (KV_SLOT >> 4);
     const uint32_t pa = tmem + static_cast<uint32_t>(2 * D + t * BN);
     const uint32_t o_tmem = tmem + static_cast<uint32_t>(t * D);
     // keys [0, BN/2) as soon as their P is stored, then the rest; when the
     // second half is already released (every softmax warp releases the
     // first half before the second), one test replaces both waits
-    const uint32_t par = static_cast<uint32_t>(j) & 1u;
     const bool all_ready = mbar_test_wait(smem_u32(&sh.p_full[t][1]), par);
     if (all_ready) tc_fence_after();
 #pragma unroll
@@ -702,45 +817,64 @@ __device__ __forceinline__ void attn_dual_mma(AttnDualShared& sh, uint32_t tmem,
     if (last) mma_commit(smem_u32(&sh.pv_done[t]));  // for the epilogue
     return true;
   };
-  bool ok = wait(&sh.q_full, 0);
-  if (ok) ok = wait(&sh.k_full[0], 0);
-  if (ok) {
-    tc_fence_after();
-    s_mma(0, 0);
-    s_mma(1, 0);
-  }
-  // ring positions: V of block j, K of block j + 1
-  int v_slot = 0, k_slot = 0;
-  uint32_t v_par = 0, k_par = 0;
-  auto step = [&](int& slot, uint32_t& parity) {
-    if (++slot == stages) {
-      slot = 0;
-      parity ^= 1u;
+  const int spans = (S + 255) / 256;
+  bool ok = true;
+  RingPos kpos, vpos;         // next K and next V block of the rings
+  uint32_t tile_blocks[2] = {0u, 0u};  // blocks of each tile so far: P phases
+  for (int it = 0; ok; ++it) {
+    int item;
+    ok = attn_dual_next_item<false>(sh, it, abort_flag, err, kErrWaitMma, item);
+    if (!ok || item < 0) break;
+    int span, bh;
+    attn_dual_item<CAUSAL>(item, spans, BH, span, bh);
+    const int q0 = span * 256;
+    const int nb0 = attn_dual_blocks<BN, CAUSAL>(S, q0, 0);
+    const int nb1 = attn_dual_blocks<BN, CAUSAL>(S, q0, 1);  // nb0 <= nb1
+    const uint32_t itp = static_cast<uint32_t>(it) & 1u;
+    // S_t(0) overwrites the S/P buffer that PV_t(last) of the previous item
+    // read; that PV was issued before, and MMAs execute in issue order
+    ok = wait(&sh.q_full, itp) && wait(&sh.k_full[kpos.slot], kpos.parity);
+    if (ok) {
+      s_mma(0, kpos.slot);
+      s_mma(1, kpos.slot);
+      kpos.step(stages);
+      if (nb1 == 1) mma_commit(smem_u32(&sh.q_empty));  // the item's last S MMAs
     }
-  };
-  step(k_slot, k_par);
-  for (int j = 0; j < nb1 && ok; ++j) {
-    if (!wait(&sh.v_full[v_slot], v_par)) {
-      ok = false;
-      break;
-    }
-    bool k_ready = false;
-#pragma unroll
-    for (int t = 0; t < 2; ++t) {
-      const int nbt = t == 0 ? nb0 : nb1;
-      if (ok && j < nbt) ok = pv_mma(t, v_slot, j, j + 1 == nbt);
-      if (ok && j + 1 < nbt) {
-        if (!k_ready) {
-          // K arrives by TMA (async proxy, like the MMA's reads): the
-          // barrier's phase alone orders it, no tcgen05 fence
-          ok = wait(&sh.k_full[k_slot], k_par);
-          k_ready = true;
-        }
-        if (ok) s_mma(t, k_slot);
+    for (int j = 0; j < nb1 && ok; ++j) {
+      if (!wait(&sh.v_full[vpos.slot], vpos.parity)) {
+        ok = false;
+        break;
       }
+      bool k_ready = false;
+#pragma unroll
+      for (int t = 0; t < 2; ++t) {
+        const int nbt = t == 0 ? nb0 : nb1;
+        if (ok && j < nbt) {
+          // PV_t(0) overwrites O_t: the previous item's epilogue must have
+          // read it out
+          if (j == 0 && it > 0) {
+            ok = wait(&sh.o_free[t], itp ^ 1u);
+            tc_fence_after();
+          }
+          if (ok) ok = pv_mma(t, vpos.slot, j, tile_blocks[t] & 1u, j + 1 == nbt);
+          ++tile_blocks[t];
+        }
+        if (ok && j + 1 < nbt) {
+          if (!k_ready) {
+            // K arrives by TMA (async proxy, like the MMA's reads): the
+            // barrier's phase alone orders it, no tcgen05 fence
+            ok = wait(&sh.k_full[kpos.slot], kpos.parity);
+            k_ready = true;
+          }
+          if (ok) {
+            s_mma(t, kpos.slot);
+            if (t == 1 && j + 2 == nb1) mma_commit(smem_u32(&sh.q_empty));
+          }
+        }
+      }
+      vpos.step(stages);
+      if (k_ready) kpos.step(stages);
     }
-    step(v_slot, v_par);
-    step(k_slot, k_par);
   }
   if (!ok) {
     mma_commit(smem_u32(&sh.drain));
@@ -748,140 +882,162 @@ __device__ __forceinline__ void attn_dual_mma(AttnDualShared& sh, uint32_t tmem,
   }
 }
 
-// Softmax and epilogue of tile t = (warp - 4) / 4; thread = query row =
-// TMEM lane.
+// Softmax and epilogue of tile t = (warp - 4) / 4 for each work item of
+// the CTA; thread = query row = TMEM lane.
 template <typename T, int FMT, int BN, int D, bool CAUSAL>
 __device__ __forceinline__ void attn_dual_softmax(AttnDualShared& sh, uint32_t tmem,
-                                                  T* __restrict__ O, int S, int q0, int bh,
-                                                  int nb0, int nb1, int stages, float scale_log2,
-                                                  int warp, int lane, volatile int* abort_flag,
-                                                  unsigned int* err) {
+                                                  T* __restrict__ O, int S, int BH, int stages,
+                                                  float scale_log2, int warp, int lane,
+                                                  volatile int* abort_flag, unsigned int* err) {
   const int t = (warp - 4) >> 2;
   const int q = warp & 3;  // TMEM lane quarter
   const int row = q * 32 + lane;
-  const int tile_first = q0 + 128 * t;
-  const int qrow = tile_first + row;
-  const int nblk = t == 0 ? nb0 : nb1;
   const uint32_t lane_addr = static_cast<uint32_t>(q * 32) << 16;
   const uint32_t sp = tmem + lane_addr + static_cast<uint32_t>(2 * D + t * BN);
   const uint32_t o_tmem = tmem + lane_addr + static_cast<uint32_t>(t * D);
   const float2 scale2 = make_float2(scale_log2, scale_log2);
-  float m_used = -INFINITY;
-  float l = 0.f;
+  const int spans = (S + 255) / 256;
   bool ok = true;
-  for (int j = 0; j < nblk; ++j) {
-    if (!mbar_wait(smem_u32(&sh.s_full[t]), static_cast<uint32_t>(j) & 1u, abort_flag, err,
-                   kErrWaitSoftmax))
-      ok = false;
+  uint32_t tb = 0;  // blocks of this tile so far (over all items): S and P phases
+  for (int it = 0; ok; ++it) {
+    int item;
+    ok = attn_dual_next_item<true>(sh, it, abort_flag, err, kErrWaitSoftmax, item);
+    if (!__all_sync(0xffffffffu, ok) || item < 0) break;
+    int span, bh;
+    attn_dual_item<CAUSAL>(item, spans, BH, span, bh);
+    const int q0 = span * 256;
+    const int tile_first = q0 + 128 * t;
+    const int qrow = tile_first + row;
+    const int nblk = attn_dual_blocks<BN, CAUSAL>(S, q0, t);
+    float m_used = -INFINITY;
+    float l = 0.f;
+    for (int j = 0; j < nblk; ++j, ++tb) {
+      if (!mbar_wait(smem_u32(&sh.s_full[t]), tb & 1u, abort_flag, err, kErrWaitSoftmax))
+        ok = false;
+      if (!__all_sync(0xffffffffu, ok)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      // MMAs complete in issue order, so S_1(j) done means every MMA before
+      // it is done: S_0(j) and S_1(j), the last readers of K(j), and the PV
+      // MMAs of block j - 1, the last readers of V(j - 1).  Tile 1 (which
+      // has every block of the span) hands both ring slots back here, with
+      // no commit on the MMA thread.
+      // (Tile 1 has every ring block of every item, so its block count is the
+      // rings' position; V of the previous item's last block is free at the
+      // first block of the next item as well.)
+      if (t == 1 && q == 0 && lane == 0) {
+        mbar_arrive(smem_u32(&sh.k_empty[tb % stages]));
+        if (tb > 0) mbar_arrive(smem_u32(&sh.v_empty[(tb - 1) % stages]));
+      }
+      uint32_t sv[BN];
+#pragma unroll
+      for (int c = 0; c < BN / 32; ++c)
+        tmem_ld32(sp + static_cast<uint32_t>(c * 32), *reinterpret_cast<uint32_t(*)[32]>(sv + c * 32));
+      tmem_wait_ld();
+      auto f = [&](int i) { return __uint_as_float(sv[i]); };
+      const int key0 = j * BN;
+      if (key0 + BN > S || (CAUSAL && key0 + BN - 1 > tile_first)) {
+#pragma unroll
+        for (int i = 0; i < BN; ++i) {
+          const int key = key0 + i;
+          if (key >= S || (CAUSAL && key > qrow)) sv[i] = __float_as_uint(-INFINITY);
+        }
+      }
+      float mx[4] = {f(0), f(1), f(2), f(3)};
+#pragma unroll
+      for (int i = 4; i + 1 < BN; i += 2) mx[(i >> 1) & 3] = fmax3(mx[(i >> 1) & 3], f(i), f(i + 1));
+      const float mb = fmaxf(fmax3(mx[0], mx[1], mx[2]), mx[3]) * scale_log2;
+      if (j == 0) {
+        m_used = mb;
+      } else {
+        const bool need = mb > m_used + kRescaleThreshold;
+        if (__any_sync(0xffffffffu, need)) {
+          const float m_new = need ? mb : m_used;
+          const float alpha = ex2_approx(m_used - m_new);
+          // O_t holds PV_t(0..j-1), complete: PV_t(j-1) was issued before
+          // S_t(j), which is done, and PV_t(j) waits for this thread's P
+#pragma unroll 1
+          for (int c = 0; c < D / 16; ++c) {
+            uint32_t r[16];
+            const uint32_t addr = o_tmem + static_cast<uint32_t>(c * 16);
+            tmem_ld16(addr, r);
+            tmem_wait_ld();
+#pragma unroll
+            for (int i = 0; i < 16; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha);
+            tmem_st16(addr, r);
+          }
+          tmem_wait_st();
+          l *= alpha;
+          m_used = m_new;
+        }
+      }
+      const float neg_m = (m_used == -INFINITY) ? 0.f : -m_used;
+      const float2 shift2 = make_float2(neg_m, neg_m);
+      float2 rs[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f),
+                      make_float2(0.f, 0.f)};
+      // P_t(j) over the first BN/2 columns of the buffer, 16 columns as soon
+      // as they are packed; the keys of each half of the block are released
+      // to the PV MMA as soon as their P is stored, so the MMA on the first
+      // half overlaps the exponentials of the second
+      auto release = [&](int h) {
+        tmem_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(smem_u32(&sh.p_full[t][h]));
+      };
+      constexpr int HALF_CHUNKS = BN / 64;  // 32-key chunks per half (0: BN 32)
+#pragma unroll
+      for (int c = 0; c < BN / 32; ++c) {
+        uint32_t pk[16];
+#pragma unroll
+        for (int g2 = 0; g2 < 16; ++g2) {
+          const int g = c * 16 + g2;
+          const float2 x = __ffma2_rn(make_float2(f(2 * g), f(2 * g + 1)), scale2, shift2);
+          const float2 p = make_float2(ex2_approx(x.x), ex2_approx(x.y));  // -inf -> 0
+          rs[g & 3] = __fadd2_rn(rs[g & 3], p);
+          pk[g2] = FMT == 1 ? pack_bf16(p.x, p.y) : pack_f16(p.x, p.y);
+        }
+        tmem_st16(sp + static_cast<uint32_t>(c * 16), pk);
+        if (c + 1 == HALF_CHUNKS) release(0);
+      }
+      const float2 rsum = __fadd2_rn(__fadd2_rn(rs[0], rs[1]), __fadd2_rn(rs[2], rs[3]));
+      l += rsum.x + rsum.y;
+      if (HALF_CHUNKS == 0) release(0);
+      release(1);
+    }
+    // ------------------------------------------------------------ epilogue
+    // pv_done[t] is committed once per item, after the tile's last PV MMA
+    if (ok && nblk > 0)
+      ok = mbar_wait(smem_u32(&sh.pv_done[t]), static_cast<uint32_t>(it) & 1u, abort_flag, err,
+                     kErrWaitSoftmax);
     if (!__all_sync(0xffffffffu, ok)) {
       ok = false;
       break;
     }
     tc_fence_after();
-    // MMAs complete in issue order, so S_1(j) done means every MMA before
-    // it is done: S_0(j) and S_1(j), the last readers of K(j), and the PV
-    // MMAs of block j - 1, the last readers of V(j - 1).  Tile 1 (which
-    // has every block of the span) hands both ring slots back here, with
-    // no commit on the MMA thread.
-    if (t == 1 && q == 0 && lane == 0) {
-      mbar_arrive(smem_u32(&sh.k_empty[j % stages]));
-      if (j > 0) mbar_arrive(smem_u32(&sh.v_empty[(j - 1) % stages]));
-    }
-    uint32_t sv[BN];
+    // O_t to registers, then hand O_t back to the MMA thread (the next item's
+    // first PV overwrites it) before normalising and storing
+    uint32_t ov[D];
 #pragma unroll
-    for (int c = 0; c < BN / 32; ++c)
-      tmem_ld32(sp + static_cast<uint32_t>(c * 32), *reinterpret_cast<uint32_t(*)[32]>(sv + c * 32));
+    for (int c = 0; c < D / 32; ++c)
+      tmem_ld32(o_tmem + static_cast<uint32_t>(c * 32),
+                *reinterpret_cast<uint32_t(*)[32]>(ov + c * 32));
     tmem_wait_ld();
-    auto f = [&](int i) { return __uint_as_float(sv[i]); };
-    const int key0 = j * BN;
-    if (key0 + BN > S || (CAUSAL && key0 + BN - 1 > tile_first)) {
+    tc_fence_before();
+    __syncwarp();
+    if (lane == 0) mbar_arrive(smem_u32(&sh.o_free[t]));
+    if (qrow < S) {
+      const float inv_l = l > 0.f ? 1.0f / l : 0.f;
+      T* orow = O + (static_cast<int64_t>(bh) * S + qrow) * D;
 #pragma unroll
-      for (int i = 0; i < BN; ++i) {
-        const int key = key0 + i;
-        if (key >= S || (CAUSAL && key > qrow)) sv[i] = __float_as_uint(-INFINITY);
-      }
-    }
-    float mx[4] = {f(0), f(1), f(2), f(3)};
-#pragma unroll
-    for (int i = 4; i + 1 < BN; i += 2) mx[(i >> 1) & 3] = fmax3(mx[(i >> 1) & 3], f(i), f(i + 1));
-    const float mb = fmaxf(fmax3(mx[0], mx[1], mx[2]), mx[3]) * scale_log2;
-    if (j == 0) {
-      m_used = mb;
-    } else {
-      const bool need = mb > m_used + kRescaleThreshold;
-      if (__any_sync(0xffffffffu, need)) {
-        const float m_new = need ? mb : m_used;
-        const float alpha = ex2_approx(m_used - m_new);
-        // O_t holds PV_t(0..j-1), complete: PV_t(j-1) was issued before
-        // S_t(j), which is done, and PV_t(j) waits for this thread's P
-#pragma unroll 1
-        for (int c = 0; c < D / 16; ++c) {
-          uint32_t r[16];
-          const uint32_t addr = o_tmem + static_cast<uint32_t>(c * 16);
-          tmem_ld16(addr, r);
-          tmem_wait_ld();
-#pragma unroll
-          for (int i = 0; i < 16; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha);
-          tmem_st16(addr, r);
-        }
-        tmem_wait_st();
-        l *= alpha;
-        m_used = m_new;
-      }
-    }
-    const float neg_m = (m_used == -INFINITY) ? 0.f : -m_used;
-    const float2 shift2 = make_float2(neg_m, neg_m);
-    float2 rs[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f),
-                    make_float2(0.f, 0.f)};
-    // P_t(j) over the first BN/2 columns of the buffer, 16 columns as soon
-    // as they are packed; the keys of each half of the block are released
-    // to the PV MMA as soon as their P is stored, so the MMA on the first
-    // half overlaps the exponentials of the second
-    auto release = [&](int h) {
-      tmem_wait_st();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(smem_u32(&sh.p_full[t][h]));
-    };
-    constexpr int HALF_CHUNKS = BN / 64;  // 32-key chunks per half (0: BN 32)
-#pragma unroll
-    for (int c = 0; c < BN / 32; ++c) {
-      uint32_t pk[16];
-#pragma unroll
-      for (int g2 = 0; g2 < 16; ++g2) {
-        const int g = c * 16 + g2;
-        const float2 x = __ffma2_rn(make_float2(f(2 * g), f(2 * g + 1)), scale2, shift2);
-        const float2 p = make_float2(ex2_approx(x.x), ex2_approx(x.y));  // -inf -> 0
-        rs[g & 3] = __fadd2_rn(rs[g & 3], p);
-        pk[g2] = FMT == 1 ? pack_bf16(p.x, p.y) : pack_f16(p.x, p.y);
-      }
-      tmem_st16(sp + static_cast<uint32_t>(c * 16), pk);
-      if (c + 1 == HALF_CHUNKS) release(0);
-    }
-    const float2 rsum = __fadd2_rn(__fadd2_rn(rs[0], rs[1]), __fadd2_rn(rs[2], rs[3]));
-    l += rsum.x + rsum.y;
-    if (HALF_CHUNKS == 0) release(0);
-    release(1);
-  }
-  // ------------------------------------------------------------ epilogue
-  // pv_done[t] is committed once, after the tile's last PV MMA
-  if (ok && nblk > 0)
-    ok = mbar_wait(smem_u32(&sh.pv_done[t]), 0u, abort_flag, err, kErrWaitSoftmax);
-  if (__all_sync(0xffffffffu, ok)) {
-    tc_fence_after();
-    const float inv_l = l > 0.f ? 1.0f / l : 0.f;
-    T* orow = O + (static_cast<int64_t>(bh) * S + qrow) * D;
-#pragma unroll 1
-    for (int c = 0; c < D / 16; ++c) {
-      uint32_t r[16];
-      tmem_ld16(o_tmem + static_cast<uint32_t>(c * 16), r);
-      tmem_wait_ld();
-      if (qrow < S) {
+      for (int c = 0; c < D / 16; ++c) {
         uint32_t pk[8];
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
-          const float lo = __uint_as_float(r[2 * i]) * inv_l;
-          const float hi = __uint_as_float(r[2 * i + 1]) * inv_l;
+          const float lo = __uint_as_float(ov[c * 16 + 2 * i]) * inv_l;
+          const float hi = __uint_as_float(ov[c * 16 + 2 * i + 1]) * inv_l;
           pk[i] = FMT == 1 ? pack_bf16(lo, hi) : pack_f16(lo, hi);
         }
         uint4* d4 = reinterpret_cast<uint4*>(orow + c * 16);
@@ -897,7 +1053,7 @@ __global__ void __launch_bounds__(kAttnDualThreads, 1)
     attn_tc_dual_kernel(const __grid_constant__ CUtensorMap tma_q,
                         const __grid_constant__ CUtensorMap tma_k,
                         const __grid_constant__ CUtensorMap tma_v, T* __restrict__ O, int BH,
-                        int S, int stages, float scale_log2, unsigned int* err) {
+                        int S, int stages, float scale_log2, int work_slot, unsigned int* err) {
   using G = AttnDualGeom<D>;
   constexpr uint32_t KV_SLOT = ((static_cast<uint32_t>(BN) * D * G::ES) + 1023u) & ~1023u;
   constexpr int COLS = 2 * D + 2 * BN;
@@ -913,31 +1069,6 @@ __global__ void __launch_bounds__(kAttnDualThreads, 1)
   const uint32_t v_smem = k_smem + static_cast<uint32_t>(stages) * KV_SLOT;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int spans = (S + 255) / 256;
-  int span, bh;
-  if constexpr (CAUSAL) {
-    // Longest spans first across groups of kAttnCausalGroup heads (one
-    // 1-D grid): the block scheduler then hands out work longest first
-    // over the whole GPU (a per-head order leaves short spans of the
-    // first heads and long spans of the last ones in the same wave), while
-    // the K/V of the heads in flight stay within L2.
-    const int i = static_cast<int>(blockIdx.x);
-    const int per_group = kAttnCausalGroup * spans;
-    const int g = i / per_group;
-    const int r = i - g * per_group;
-    const int gh = min(kAttnCausalGroup, BH - g * kAttnCausalGroup);
-    span = spans - 1 - r / gh;
-    bh = g * kAttnCausalGroup + r % gh;
-  } else {
-    span = static_cast<int>(blockIdx.x);
-    bh = static_cast<int>(blockIdx.y);
-  }
-  const int q0 = span * 256;  // tile t: query rows [q0 + 128 t, +128)
-  auto blocks_of = [&](int t) {
-    const int len = CAUSAL ? min(S, q0 + 128 * (t + 1)) : S;
-    return (len + BN - 1) / BN;
-  };
-  const int nb0 = blocks_of(0), nb1 = blocks_of(1);  // nb0 <= nb1
 
   if (threadIdx.x == 0) {
     mbar_init(smem_u32(&sh.q_full), 1);
@@ -952,6 +1083,12 @@ __global__ void __launch_bounds__(kAttnDualThreads, 1)
       mbar_init(smem_u32(&sh.p_full[t][0]), 4);
       mbar_init(smem_u32(&sh.p_full[t][1]), 4);
       mbar_init(smem_u32(&sh.pv_done[t]), 1);
+      mbar_init(smem_u32(&sh.o_free[t]), 4);
+    }
+    mbar_init(smem_u32(&sh.q_empty), 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(smem_u32(&sh.item_full[i]), 1);
+      mbar_init(smem_u32(&sh.item_empty[i]), kAttnItemReaders);
     }
     mbar_init(smem_u32(&sh.drain), 1);
     sh.abort = 0;
@@ -974,21 +1111,30 @@ __global__ void __launch_bounds__(kAttnDualThreads, 1)
   if (warp < 4) {
     regs_dec<kAttnDualLowRegs>();
     if ((warp == 0 || warp == 3) && lane == 0)
-      attn_dual_producer<BN, D>(&tma_q, warp == 0 ? &tma_k : &tma_v, sh, q_smem,
-                                warp == 0 ? k_smem : v_smem, q0, bh, nb1, stages, warp == 0,
-                                abort_flag, err);
+      attn_dual_producer<BN, D, CAUSAL>(&tma_q, warp == 0 ? &tma_k : &tma_v, sh, q_smem,
+                                        warp == 0 ? k_smem : v_smem, S, BH, stages, work_slot,
+                                        warp == 0, abort_flag, err);
     else if (warp == 1 && lane == 0)
-      attn_dual_mma<FMT, BN, D>(sh, tmem, q_smem, k_smem, v_smem, nb0, nb1, stages, abort_flag,
-                                err);
+      attn_dual_mma<FMT, BN, D, CAUSAL>(sh, tmem, q_smem, k_smem, v_smem, S, BH, stages,
+                                        abort_flag, err);
   } else {
     regs_inc<kAttnDualHighRegs>();
-    attn_dual_softmax<T, FMT, BN, D, CAUSAL>(sh, tmem, O, S, q0, bh, nb0, nb1, stages,
-                                             scale_log2, warp, lane, abort_flag, err);
+    attn_dual_softmax<T, FMT, BN, D, CAUSAL>(sh, tmem, O, S, BH, stages, scale_log2, warp, lane,
+                                             abort_flag, err);
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   if (warp == 2) tmem_dealloc(tmem, ALLOC);
+  if (threadIdx.x == 0) {
+    // every CTA has taken its last item before it counts itself done, so the
+    // last one can clear the slot
+    unsigned int* work = g_attn_work[work_slot];
+    if (atomicAdd(&work[1], 1u) == gridDim.x - 1) {
+      atomicExch(&work[0], 0u);
+      atomicExch(&work[1], 0u);
+    }
+  }
 }
 
 // ------------------------------------------------------------------- host
@@ -1069,10 +1215,10 @@ static gpo_status plan_attention_dual(const gpo_key& k, Plan& p, std::string& lo
   p.res.smem_bytes = smem;
   p.res.tmem_cols = static_cast<uint32_t>(attn_tmem_alloc(cols));
   p.res.threads_per_cta = static_cast<uint32_t>(kAttnDualThreads);
-  const bool causal = k.task == GPO_TASK_ATTENTION_CAUSAL;
-  p.res.grid_x = static_cast<uint32_t>(cdiv(k.shape[1], 256) * (causal ? k.shape[0] : 1));
-  p.res.grid_y = static_cast<uint32_t>(causal ? 1 : k.shape[0]);
-  p.res.grid_z = 1;
+  // persistent: one CTA per SM at launch, at most one per work item
+  p.res.grid_x = static_cast<uint32_t>(cdiv(k.shape[1], 256) * k.shape[0]);
+  p.res.grid_y = p.res.grid_z = 1;
+  p.res.persistent = 1u;
   p.res.launches_per_call = 1;
   snprintf(p.res.kernel, sizeof(p.res.kernel), "attn_tc_dual_kernel<%s,BN=%d,D=%d,%s,two_tiles>",
            k.dtype == GPO_BFLOAT16 ? "bf16" : "f16", BN, D,
@@ -1189,12 +1335,17 @@ static gpo_status run_attn_tc_dual(const gpo_key& k, const Plan& p, const gpo_ar
   const uint32_t dyn = static_cast<uint32_t>(p.aux[0]);
   gpo_status s = ensure_smem_attr(reinterpret_cast<const void*>(kern), dyn);
   if (s != GPO_OK) return s;
-  const dim3 grid = CAUSAL ? dim3(static_cast<unsigned>(cdiv(S, 256) * BH), 1)
-                           : dim3(static_cast<unsigned>(cdiv(S, 256)), static_cast<unsigned>(BH));
+  // persistent CTAs (one per SM: shared memory and TMEM) taking (span,
+  // head) items from the launch's work counter
+  const uint64_t items = cdiv(S, 256) * BH;
+  const dim3 grid(static_cast<unsigned>(
+      std::min<uint64_t>(items, static_cast<uint64_t>(c.sm_count > 0 ? c.sm_count : 148))));
   const float scale_log2 = 1.4426950408889634f / sqrtf(static_cast<float>(D));
+  static std::atomic<unsigned> launches{0};
+  const int work_slot = static_cast<int>(launches.fetch_add(1u) % kAttnWorkSlots);
   kern<<<grid, kAttnDualThreads, dyn, c.stream>>>(mq, mk, mv, static_cast<T*>(a.out),
                                                   static_cast<int>(BH), static_cast<int>(S),
-                                                  k.num_stages, scale_log2, c.err);
+                                                  k.num_stages, scale_log2, work_slot, c.err);
   return launch_status();
 }
 

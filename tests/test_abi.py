@@ -110,7 +110,7 @@ def test_attention_plans():
     assert rd["grid"] == [16 * 128, 1, 1] and rd["threads_per_cta"] == 384
     rf = compile_module("attention", (128, 4096, 128),
                         {**base, "BLOCK_M": 256, "num_warps": 8}).resources()
-    assert rf["grid"] == [16, 128, 1]
+    assert rf["grid"] == [16 * 128, 1, 1] and rf["persistent"]
     assert rd["tmem_cols"] == 512 and rd["smem_bytes"] <= 227 * 1024
     for bad in ({"num_stages": 3}, {"BLOCK_N": 128, "num_stages": 4}):  # shared memory
         with pytest.raises(KernelBuildError, match="shared memory"):
