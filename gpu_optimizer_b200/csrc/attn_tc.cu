@@ -595,9 +595,9 @@ static_assert(128 * kAttnDualLowRegs + 256 * kAttnDualHighRegs <= 168 * kAttnDua
 constexpr int kAttnWorkSlots = 64;
 __device__ unsigned int g_attn_work[kAttnWorkSlots][2];
 
-// Work item i: the 256-row query span and head it covers.  Full attention walks the
-// spans of one head after another, so the CTAs in flight share the K/V of
-// a few heads in L2.  Causal spans go longest first across groups of
+// Work item i: the 256-row query span and head it covers.  Full attention
+// walks the spans of one head after another, so the CTAs in flight share
+// the K/V of a few heads in L2.  Causal spans go longest first across groups of
 // kAttnCausalGroup heads: items are then handed out longest first over the
 // whole GPU (a per-head order leaves short spans of the first heads and
 // long spans of the last ones in the same wave), while the K/V of the heads
