@@ -537,8 +537,9 @@ __global__ void __launch_bounds__(128 + 128 * WG,
 // 128-row query tiles, t = 0 and 1, that share every K/V block.  The next
 // item's Q load and first S MMAs run under the current item's epilogue (Q
 // is reloaded once the item's last S MMAs are done, O_t is rewritten once
-// the epilogue has read it), and the K/V rings run on across items.  TMEM holds O_t in columns [t*D, t*D + D) and one S/P buffer per
-// tile in [2D + t*BN, 2D + (t+1)*BN).  The MMA thread alternates the tiles
+// the epilogue has read it), and the K/V rings run on across items.  TMEM
+// holds O_t in columns [t*D, t*D + D) and one S/P buffer per tile in
+// [2D + t*BN, 2D + (t+1)*BN).  The MMA thread alternates the tiles
 //     ... PV_0(j), S_0(j+1), PV_1(j), S_1(j+1), PV_0(j+1), S_0(j+2) ...
 // so while softmax warpgroup t turns S_t(j) into P_t(j), the tensor pipe
 // runs the other tile's PV and S MMAs: each tile's chain S -> softmax -> PV
