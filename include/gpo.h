@@ -24,7 +24,11 @@
  *    The library keeps one 256-byte device error word per device, allocated
  *    on the first launch on that device.
  *  - Modules are immutable after gpo_compile and may be shared by host
- *    threads; launches on different streams may run concurrently.
+ *    threads; launches on different streams may run concurrently.  The
+ *    persistent two-tile attention kernel (BLOCK_M 256, num_warps 8) takes
+ *    its work items from one of 64 counters in the library, chosen per
+ *    launch in turn: at most 64 of its launches may overlap on one device,
+ *    and replays of one captured graph must not overlap each other.
  */
 #ifndef GPO_H_
 #define GPO_H_
