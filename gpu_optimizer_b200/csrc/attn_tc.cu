@@ -943,11 +943,12 @@ __device__ __forceinline__ void attn_dual_softmax(AttnDualShared& sh, uint32_t t
       auto f = [&](int i) { return __uint_as_float(sv[i]); };
       const int key0 = j * BN;
       if (key0 + BN > S || (CAUSAL && key0 + BN - 1 > tile_first)) {
+        // keys key0 + i with i <= last are visible (i is a constant of the
+        // unrolled loop: one compare and one select per score)
+        const int last = CAUSAL ? min(S - 1, qrow) - key0 : S - 1 - key0;
 #pragma unroll
-        for (int i = 0; i < BN; ++i) {
-          const int key = key0 + i;
-          if (key >= S || (CAUSAL && key > qrow)) sv[i] = __float_as_uint(-INFINITY);
-        }
+        for (int i = 0; i < BN; ++i)
+          if (i > last) sv[i] = __float_as_uint(-INFINITY);
       }
       float mx[4] = {f(0), f(1), f(2), f(3)};
 #pragma unroll
