@@ -795,6 +795,8 @@ __device__ __forceinline__ void attn_dual_mma(AttnDualShared& sh, uint32_t tmem,
                  kk > 0 ? 1u : 0u);
     }
     mma_commit(smem_u32(&sh.s_full[t]));
+    // S_1 is the last reader of a K block (S_0 of it was issued before)
+    if (t == 1) mma_commit(smem_u32(&sh.k_empty[k_slot]));
   };
   // P_t sits in the first BN/2 columns of tile t's S/P buffer
   auto pv_mma = [&](int t, int v_slot, int j, uint32_t par, bool last) {
@@ -819,6 +821,8 @@ __device__ __forceinline__ void attn_dual_mma(AttnDualShared& sh, uint32_t tmem,
                    (j > 0 || kk > 0) ? 1u : 0u);
     }
     if (last) mma_commit(smem_u32(&sh.pv_done[t]));  // for the epilogue
+    // PV_1 is the last reader of a V block (PV_0 of it was issued before)
+    if (t == 1) mma_commit(smem_u32(&sh.v_empty[v_slot]));
     return true;
   };
   const int spans = (S + 255) / 256;
@@ -923,18 +927,6 @@ __device__ __forceinline__ void attn_dual_softmax(AttnDualShared& sh, uint32_t t
         break;
       }
       tc_fence_after();
-      // MMAs complete in issue order, so S_1(j) done means every MMA before
-      // it is done: S_0(j) and S_1(j), the last readers of K(j), and the PV
-      // MMAs of block j - 1, the last readers of V(j - 1).  Tile 1 (which
-      // has every block of the span) hands both ring slots back here, with
-      // no commit on the MMA thread.
-      // (Tile 1 has every ring block of every item, so its block count is the
-      // rings' position; V of the previous item's last block is free at the
-      // first block of the next item as well.)
-      if (t == 1 && q == 0 && lane == 0) {
-        mbar_arrive(smem_u32(&sh.k_empty[tb % stages]));
-        if (tb > 0) mbar_arrive(smem_u32(&sh.v_empty[(tb - 1) % stages]));
-      }
       uint32_t sv[BN];
 #pragma unroll
       for (int c = 0; c < BN / 32; ++c)
