@@ -894,7 +894,7 @@ __device__ __forceinline__ void attn_dual_mma(AttnDualShared& sh, uint32_t tmem,
 // the CTA; thread = query row = TMEM lane.
 template <typename T, int FMT, int BN, int D, bool CAUSAL>
 __device__ __forceinline__ void attn_dual_softmax(AttnDualShared& sh, uint32_t tmem,
-                                                  T* __restrict__ O, int S, int BH, int stages,
+                                                  T* __restrict__ O, int S, int BH,
                                                   float scale_log2, int warp, int lane,
                                                   volatile int* abort_flag, unsigned int* err) {
   const int t = (warp - 4) >> 2;
@@ -1116,7 +1116,7 @@ __global__ void __launch_bounds__(kAttnDualThreads, 1)
                                         abort_flag, err);
   } else {
     regs_inc<kAttnDualHighRegs>();
-    attn_dual_softmax<T, FMT, BN, D, CAUSAL>(sh, tmem, O, S, BH, stages, scale_log2, warp, lane,
+    attn_dual_softmax<T, FMT, BN, D, CAUSAL>(sh, tmem, O, S, BH, scale_log2, warp, lane,
                                              abort_flag, err);
   }
   tc_fence_before();
