@@ -483,14 +483,20 @@ gpo_status plan_matmul(const gpo_key& k, Plan& p, std::string& log) {
   }
   const int es = dtype_bytes(k.dtype);
   const bool tc_dtype = k.dtype != GPO_FLOAT32;
-  const bool tc_tile = (k.block_m == 64 || k.block_m == 128 || k.block_m == 256) &&
-                       k.block_n >= 32 && k.block_k * es >= 32 &&
-                       (k.num_warps == 4 || k.num_warps == 8);
+  const bool tc_tile =
+      (k.block_m == 32 || k.block_m == 64 || k.block_m == 128 || k.block_m == 256) &&
+      k.block_n >= 32 && k.block_k * es >= 32 && (k.num_warps == 4 || k.num_warps == 8);
   const bool tc_shape = (k.shape[2] * es) % 16 == 0 && (k.shape[1] * es) % 16 == 0;
   if (tc_dtype && tc_tile && tc_shape) {
     gpo_status s = plan_matmul_tc(k, p, log);
-    p.aux[7] = 1;
-    return s;
+    // BLOCK_M 32 stages A in 64-row atoms on the tensor cores; where that
+    // does not fit, the CUDA-core tile (32-row A) still may
+    if (!(k.block_m == 32 && s == GPO_COMPILE_ERROR)) {
+      p.aux[7] = 1;
+      return s;
+    }
+    p = Plan{};
+    log.clear();
   }
   p.aux[7] = 0;
   return plan_matmul_simt(k, p, log);

@@ -7,7 +7,11 @@
 // (runner.py:101), fp32 accumulation in TMEM.
 //
 // Config mapping (one instantiation per (dtype, BLOCK_M, BLOCK_N, warps)):
-//   BLOCK_M    : 64  -> one M=64 MMA per K step; D row
+//   BLOCK_M    : 32  -> the M=64 MMA over A atoms of 64 rows of which TMA
+//                fills the tile's 32 (the other 32 rows are never stored:
+//                an MMA output row depends only on its own A row), so the
+//                epilogue's first two warps store 16 rows each.
+//                64  -> one M=64 MMA per K step; D row
 //                16g + r sits in TMEM lane 32g + r (g < 4, r < 16), so each
 //                epilogue warp stores 16 rows.
 //                128 -> one M=128 MMA per K step (matmul_tc_kernel).
@@ -159,7 +163,8 @@ __global__ void __launch_bounds__(PERSISTENT ? 256 : 128, 1)
   constexpr int SWB = (BN * ES) < 128 ? (BN * ES) : 128;
   // BLOCK_M 64: one M=64 MMA per K step; its D rows 16g..16g+15 land in
   // TMEM lanes 32g..32g+15 (g = 0..3), columns as N (measured layout)
-  constexpr int MMA_M = BM < 128 ? BM : 128;
+  constexpr int AROWS = BM < 64 ? 64 : BM;  // rows of an A atom in shared memory
+  constexpr int MMA_M = AROWS < 128 ? AROWS : 128;
   constexpr int HALVES = BM < 128 ? 1 : BM / 128;
   constexpr int COLS = HALVES * BN;  // TMEM columns per accumulator buffer
   constexpr int ACC_STAGES = (PERSISTENT && 2 * COLS <= 512) ? 2 : 1;
@@ -174,7 +179,8 @@ __global__ void __launch_bounds__(PERSISTENT ? 256 : 128, 1)
   __shared__ TcShared sh;
   extern __shared__ uint8_t dyn_smem[];
   const uint32_t smem_base = (smem_u32(dyn_smem) + 1023u) & ~1023u;
-  const uint32_t a_bytes = static_cast<uint32_t>(BM) * BK * ES;
+  const uint32_t a_bytes = static_cast<uint32_t>(AROWS) * BK * ES;  // shared memory
+  const uint32_t a_tx = static_cast<uint32_t>(BM) * BK * ES;         // loaded by TMA
   const uint32_t b_bytes = static_cast<uint32_t>(BK) * BN * ES;
   const uint32_t stage_bytes = (a_bytes + b_bytes + 1023u) & ~1023u;
 
@@ -226,12 +232,12 @@ __global__ void __launch_bounds__(PERSISTENT ? 256 : 128, 1)
           break;
         }
         const uint32_t full = smem_u32(&sh.full[s]);
-        mbar_arrive_expect_tx(full, a_bytes + b_bytes);
+        mbar_arrive_expect_tx(full, a_tx + b_bytes);
         const uint32_t sa = smem_base + s * stage_bytes;
         const uint32_t sb = sa + a_bytes;
         const int a_atoms = (BK * ES) / swa;
         for (int a = 0; a < a_atoms; ++a)
-          tma_load_2d(sa + a * BM * swa, &tma_a, full, kb * BK + a * (swa / ES), pm * BM);
+          tma_load_2d(sa + a * AROWS * swa, &tma_a, full, kb * BK + a * (swa / ES), pm * BM);
 #pragma unroll
         for (int c = 0; c < (BN * ES) / SWB; ++c)
           tma_load_2d(sb + c * BK * SWB, &tma_b, full, pn * BN + c * (SWB / ES), kb * BK);
@@ -284,8 +290,8 @@ __global__ void __launch_bounds__(PERSISTENT ? 256 : 128, 1)
         }
         tc_fence_after();
         const uint32_t so4 = (static_cast<uint32_t>(s) * stage_bytes) >> 4;
-        issue_kblock_any<ES, BM, SWB, HALVES, BN, FMT, false>(ksteps, d_tmem, adesc0 + so4,
-                                                              bdesc0 + so4, IDESC, kb == 0);
+        issue_kblock_any<ES, AROWS, SWB, HALVES, BN, FMT, false>(ksteps, d_tmem, adesc0 + so4,
+                                                                 bdesc0 + so4, IDESC, kb == 0);
         mma_commit(smem_u32(&sh.empty[s]));  // stage reusable once these MMAs finish
         if (++s == stages) {
           s = 0;
@@ -318,8 +324,9 @@ __global__ void __launch_bounds__(PERSISTENT ? 256 : 128, 1)
       tile_coords(tile, num_pid_m, num_pid_n, group_m, pm, pn);
 #pragma unroll
       for (int h = 0; h < HALVES; ++h) {
-        // BLOCK_M 64: lanes 16..31 of each quarter hold no row
-        const int row = BM < 128 ? (lane < 16 ? pm * BM + q * 16 + lane : M)
+        // BLOCK_M 64: lanes 16..31 of each quarter hold no row; BLOCK_M 32:
+        // quarters 2 and 3 hold only the rows past the tile
+        const int row = BM < 128 ? (lane < 16 && q * 16 < BM ? pm * BM + q * 16 + lane : M)
                                  : pm * BM + h * 128 + q * 32 + lane;
 #pragma unroll 1
         for (int c = 0; c < BN / 32; ++c) {
@@ -665,8 +672,8 @@ gpo_status plan_matmul_tc(const gpo_key& k, Plan& p, std::string& log) {
   const int es = dtype_bytes(k.dtype);
   const int BM = k.block_m, BN = k.block_n, BK = k.block_k;
   const int64_t M = k.shape[0], N = k.shape[1], K = k.shape[2];
-  if (BM != 64 && BM != 128 && BM != 256) {
-    log = "tcgen05 family needs BLOCK_M 64, 128 or 256";
+  if (BM != 32 && BM != 64 && BM != 128 && BM != 256) {
+    log = "tcgen05 family needs BLOCK_M 32, 64, 128 or 256";
     return GPO_BAD_CONFIG;
   }
   if (BN != 32 && BN != 64 && BN != 128 && BN != 256) {
@@ -737,7 +744,8 @@ gpo_status plan_matmul_tc(const gpo_key& k, Plan& p, std::string& log) {
     return GPO_OK;
   }
   p.aux[3] = 0;
-  const uint32_t a_bytes = static_cast<uint32_t>(BM) * BK * es;
+  // BLOCK_M 32 stages A in the 64-row atoms of the M=64 MMA
+  const uint32_t a_bytes = static_cast<uint32_t>(std::max(BM, 64)) * BK * es;
   const uint32_t b_bytes = static_cast<uint32_t>(BK) * BN * es;
   const uint32_t stage = (a_bytes + b_bytes + 1023u) & ~1023u;
   const uint32_t dyn = stage * static_cast<uint32_t>(k.num_stages) + 1024u;
@@ -917,6 +925,9 @@ static gpo_status run_tc_dt(const gpo_key& k, const Plan& p, const gpo_args& a,
                             const LaunchCtx& c, CUtensorMapDataType dt) {
   if (p.aux[3]) return run_tc2_bn<T, FMT>(k, p, a, c, dt);
   const bool P = p.aux[2] != 0;
+  if (k.block_m == 32)
+    return P ? run_tc_bn<T, FMT, 32, true>(k, p, a, c, dt)
+             : run_tc_bn<T, FMT, 32, false>(k, p, a, c, dt);
   if (k.block_m == 64)
     return P ? run_tc_bn<T, FMT, 64, true>(k, p, a, c, dt)
              : run_tc_bn<T, FMT, 64, false>(k, p, a, c, dt);

@@ -77,8 +77,24 @@ def test_simt_register_tile_overflow_is_a_compile_error():
 
 
 def test_small_tiles_route_to_cuda_cores():
+    # fp32 and 16-row tiles run on the CUDA cores
+    res = mm({"BLOCK_M": 32, "BLOCK_N": 32, "BLOCK_K": 16, "num_warps": 4,
+              "dtype": "float32"}).resources()
+    assert res["kernel"].startswith("matmul_simt")
+    res = mm({"BLOCK_M": 16, "BLOCK_N": 32, "BLOCK_K": 16, "num_warps": 4}).resources()
+    assert res["kernel"].startswith("matmul_simt")
+
+
+def test_block_m_32_runs_on_tensor_cores_with_cuda_core_fallback():
+    # 16-bit BLOCK_M 32: the M=64 MMA over 64-row A atoms
     res = mm({"BLOCK_M": 32, "BLOCK_N": 32, "BLOCK_K": 16, "num_warps": 4}).resources()
-    assert res["kernel"].startswith("matmul_simt_kernel")
+    assert res["kernel"] == "matmul_tc_kernel<bf16,32,32,tile>"
+    assert res["grid"][0] == (4096 // 32) * (4096 // 32)
+    # A in 64-row atoms: 5 stages x (64 + 32) x 256 bf16 do not fit; the
+    # CUDA-core tile (32-row A) does, so the config still compiles
+    cfg = {"BLOCK_M": 32, "BLOCK_N": 32, "BLOCK_K": 256, "num_warps": 4, "num_stages": 5}
+    res = mm(cfg).resources()
+    assert res["kernel"].startswith("matmul_simt"), res["kernel"]
 
 
 def test_attention_plans():

@@ -57,6 +57,9 @@ MM_TC = [  # tcgen05 family: (BM, BN, BK, GROUP_M, warps, stages)
     # BLOCK_M 64: M=64 MMAs
     (64, 128, 64, 8, 4, 4), (64, 256, 64, 8, 8, 4), (64, 64, 32, 1, 4, 3),
     (64, 32, 128, 4, 8, 2),
+    # BLOCK_M 32: M=64 MMAs over 64-row A atoms holding the tile's 32 rows
+    (32, 128, 64, 8, 4, 3), (32, 64, 64, 1, 8, 4), (32, 256, 32, 4, 4, 2),
+    (32, 32, 128, 1, 8, 2),
 ]
 MM_SIMT = [(16, 16, 16, 1, 2, 2), (32, 32, 16, 1, 4, 2), (64, 128, 32, 4, 8, 3),
            (128, 128, 64, 8, 8, 4)]
