@@ -39,7 +39,8 @@ def relative_cost(cand: Candidate) -> float:
     A CUDA-core tile of a x b outputs per thread does a*b FMAs per a + b
     operands it reads from shared memory, so its time per FLOP scales as
     (a + b) / (a * b); the register-prefetch form (no cp.async pipeline)
-    is slower again."""
+    is slower again.  A tensor-core tile of BLOCK_M 32 runs the M=64 MMA
+    with half of its rows unused, so it counts twice."""
     import re
 
     from .runner import KernelBuildError, compile_module
@@ -53,7 +54,8 @@ def relative_cost(cand: Candidate) -> float:
         a, b = (int(m.group(1)), int(m.group(2))) if m else (8, 8)
         cost = 120.0 * (a + b) / (a * b)  # 30 for an 8 x 8 tile
         return cost if "async" in kernel else 1.3 * cost
-    return 3.0 if cand.config.get("dtype") == "tf32" else 1.0
+    cost = 3.0 if cand.config.get("dtype") == "tf32" else 1.0
+    return cost * max(1.0, 64.0 / float(cand.config.get("BLOCK_M", 64)))
 
 
 def longest_first(candidates: Sequence[Candidate]) -> list[int]:

@@ -168,3 +168,8 @@ def test_longest_first_order_from_the_plan():
     tf32 = Candidate("matmul", shape, {**base, "BLOCK_M": 128, "BLOCK_N": 128, "dtype": "tf32"})
     assert relative_cost(refused) == 0.0
     assert longest_first([tc, refused, simt, tf32]) == [2, 3, 0, 1]
+    # a BLOCK_M 32 tensor-core tile uses half of each M=64 MMA
+    tc32 = Candidate("matmul", shape, {**base, "BLOCK_M": 32, "BLOCK_N": 128,
+                                       "dtype": "bfloat16"})
+    assert relative_cost(tc32) == 2.0 * relative_cost(tc)
+    assert longest_first([tc, tc32]) == [1, 0]
