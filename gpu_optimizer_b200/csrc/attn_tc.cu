@@ -4,7 +4,10 @@
 // Replaces attention_kernel (compiler/triton/kernels.py:212-270) for 16-bit
 // inputs with BLOCK_M = 64, 128 or 256.  One CTA per (128-row query tile,
 // batch*head) -- 64-row tiles with M=64 MMAs for BLOCK_M 64, a CTA pair on
-// two tiles for 256; causal grids visit the longest query tiles first.
+// two tiles for 256 with 4 warps; causal grids visit the longest query
+// tiles first.  BLOCK_M 256 with 8 warps is the persistent two-tile kernel
+// further down (its own section describes it); the roles below are those
+// of the one-tile kernel.
 //
 // Warp roles:
 //   warp 0  TMA producer of Q (once) and of the K ring (num_stages slots).
